@@ -1,0 +1,300 @@
+"""Benchmark: batched top-p sampling of B x 32000 fp32 logits on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one pass of the logits -> token path over one batch: the top-p
+workload (per GPU B=4096 rows x V=32000, Gumbel + Zipf-bonus logits,
+T=0.7, topp 0.9/0.95 by row, per-row xorshift seeds 42 + global row).  With N
+GPUs (torchrun, one process per GPU) every rank samples its own 4096 rows
+(weak scaling; rows are independent, no collective on the data path).
+
+`value` is device-timed (CUDA events, inputs resident in HBM, 524 MB per
+step > the 126 MB L2, so no flush is needed), max over ranks.  `e2e` is the
+same metric through the host-buffer C-ABI entry point (sampler_batched_host)
+with the H2D copy of the logits from pinned memory and the D2H copy of the
+ids inside the timed region.  `--impl reference` times the reference's own
+CPU sampler (llama2.c sample() over rows, OpenMP over the host cores).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+ROWS_PER_GPU = 4096
+VOCAB = 32000
+TEMP = 0.7
+METRIC = "sampled tokens/sec & HBM GB/s, B×32000 fp32 logits, top-p 0.9, at 1/2/4/8 B200"
+WORKLOAD = "top-p batch: B=4096 per GPU x V=32000 fp32, Gumbel+Zipf(1.1) logits, T=0.7, topp 0.9/0.95 by row"
+
+
+def load_json(path, default=None):
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return default
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_rows(rank, rows=ROWS_PER_GPU):
+    """Rank 0 gets exactly the seeded top-p workload; rank r>0 draws its rows
+    from the same generator recipe with seed 3000 + r."""
+    from __graft_entry__ import load_package
+    wl = load_package().workloads
+    if rank == 0:
+        w = wl.topp(rows=rows)
+    else:
+        import numpy.random as npr
+        rng = npr.default_rng(3000 + rank)
+        x = np.empty((rows, VOCAB), dtype=np.float32)
+        ranks = np.arange(1, VOCAB + 1, dtype=np.float64) ** -1.1
+        for r in range(rows):
+            g = rng.gumbel(0.0, 1.0, size=VOCAB)
+            a = rng.uniform(0.0, 12.0)
+            perm = rng.permutation(VOCAB)
+            b = np.empty(VOCAB)
+            b[perm] = a * ranks
+            x[r] = (g + b).astype(np.float32)
+        w = dict(logits=x, topp_rows=np.where(np.arange(rows) % 2 == 0, 0.9, 0.95).astype(np.float32))
+    return w["logits"], w["topp_rows"]
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during timing."""
+
+    def __init__(self, gpu_index):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(x, topp_rows, rows, use_ref=True):
+    """The reference's own sampler over `rows` rows on all host threads."""
+    import oracle
+    if use_ref and oracle.ref_available():
+        lib, kind = oracle.ref_sampler(), "reference"
+        threads = lib.num_threads()
+    else:
+        lib, kind = oracle.oracle(), "port"
+        threads = os.cpu_count()
+    from __graft_entry__ import load_package
+    seeds = load_package().workloads.row_seeds(rows)
+    t0 = time.perf_counter()
+    lib.sample_batch(x[:rows], TEMP, 0.9, seeds, topp_rows=topp_rows[:rows], nthreads=threads)
+    dt = time.perf_counter() - t0
+    return dict(value=rows / dt, unit="tokens/s", cores=threads, kind=kind,
+                sample=f"{rows} rows of the top-p workload (llama2.c sample() per row, OpenMP over rows), {dt:.2f} s")
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU sampler on the same workload."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    rows = args.ref_rows
+    x, tr = make_rows(0, rows=rows)
+    import oracle
+    if not oracle.ref_available():
+        oracle.build(with_ref=True)
+    kind = "reference" if oracle.ref_available() else "port"
+    lib = oracle.ref_sampler() if kind == "reference" else oracle.oracle()
+    threads = lib.num_threads() if kind == "reference" else os.cpu_count()
+    from __graft_entry__ import load_package
+    seeds = load_package().workloads.row_seeds(rows)
+    for _ in range(args.warmup):
+        lib.sample_batch(x, TEMP, 0.9, seeds, topp_rows=tr, nthreads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        lib.sample_batch(x, TEMP, 0.9, seeds, topp_rows=tr, nthreads=threads)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = rows / dt
+    line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
+                ms_per_step=dt * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f32",
+                data="synthetic (seeded numpy PCG64)", impl="reference",
+                config=dict(workload=WORKLOAD, rows_per_step=rows, vocab=VOCAB, parallelism="host threads"),
+                cpu_baseline=dict(value=value, unit="tokens/s", cores=threads, kind=kind,
+                                  sample=f"{rows} rows per step, llama2.c sample() per row, OpenMP over rows"),
+                e2e=dict(value=value, unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    pkg = load_package()
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    x_host, topp_host = make_rows(rank)
+    B = x_host.shape[0]
+    row0 = rank * B
+    seeds = pkg.workloads.row_seeds(B, offset=row0)
+    x = torch.from_numpy(x_host).to(dev)
+    topp_rows = torch.from_numpy(topp_host).to(dev)
+    states = torch.empty(B, dtype=torch.int64, device=dev)
+    ids = torch.empty(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        pkg.seed_states(states, 42, row0)
+        pkg.sample_batched(x, TEMP, 0.9, states, topp_rows=topp_rows, out_ids=ids, stream=stream)
+        return pkg.last_launch_count() + 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    time.sleep(0.25)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    ev0.record(stream)
+    for _ in range(args.steps):
+        launches += step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    # per-launch duration of the row kernel alone (events around each launch)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    pkg.seed_states(states, 42, row0)
+    for a, b in kev:
+        a.record(stream)
+        pkg.sample_batched(x, TEMP, 0.9, states, topp_rows=topp_rows, out_ids=ids, stream=stream)
+        b.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    kernel_ms = float(np.mean([a.elapsed_time(b) for a, b in kev]))
+    t = torch.tensor([ms, kernel_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, kernel_ms = float(t[0]), float(t[1])
+
+    # end to end through the host-buffer C-ABI call: pinned logits in,
+    # ids and states out, copies inside the timed region
+    pin = torch.from_numpy(x_host).pin_memory()
+    xh = pin.numpy()
+    st_host = np.empty(B, dtype=np.uint64)
+    e2e_steps = max(1, min(args.steps, 10))
+    for _ in range(2):
+        st_host[:] = seeds
+        pkg.sample_batched_host(xh, TEMP, 0.9, st_host, topp_rows_np=topp_host)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        st_host[:] = seeds
+        pkg.sample_batched_host(xh, TEMP, 0.9, st_host, topp_rows_np=topp_host)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms)
+
+    if rank == 0:
+        peaks = load_json(os.path.join(ROOT, "MEASURED_PEAKS.json"), {})
+        peak = peaks.get("hbm_gbs")
+        peak_note = "of measured"
+        if not peak:
+            peak, peak_note = 6650.0, "of fallback"
+        alg_bytes = B * VOCAB * 4 + B * (8 + 8 + 4 + 4)  # logits + state r/w + topp + ids
+        achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
+        traffic = load_json(os.path.join(ROOT, "profiles", "row_sampler_traffic.json"), {}).get("bytes_per_launch")
+        cpu = None
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline(x_host, topp_host, args.cpu_rows)
+        value = world * B / (ms * 1e-3)
+        line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak", vs_baseline=None,
+                    dtype="f32", data="synthetic (seeded numpy PCG64: Gumbel + Zipf(1.1) ranked bonus)",
+                    config=dict(workload=WORKLOAD, global_batch=world * B, rows_per_gpu=B, vocab=VOCAB,
+                                temperature=TEMP, parallelism=f"rows sharded over {world} GPU(s), no collective",
+                                l2="inputs 524 MB per GPU > 126 MB L2; no flush"),
+                    hbm_gbs=world * alg_bytes / (ms * 1e-3) / 1e9,
+                    roofline=dict(bound="hbm", achieved=achieved, peak=peak, unit="GB/s", frac=achieved / peak,
+                                  traffic=traffic, kernel="row_sampler_kernel", kernel_ms=kernel_ms,
+                                  peak_source=peak_note),
+                    cpu_baseline=cpu,
+                    e2e=dict(value=world * B / (e2e_ms * 1e-3), unit="tokens/s",
+                             h2d_bytes_per_step=B * VOCAB * 4 + B * 12, d2h_bytes_per_step=B * 12,
+                             ms_per_step=e2e_ms),
+                    gpu_launches=launches, clocks=clk)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--ref-rows", type=int, default=512)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,178 @@
+/*
+ * b200_sampler.h -- C-ABI of the B200 (sm_100a) logits -> token sampler.
+ *
+ * Part 1 is the llama2.c Sampler surface, kept as a drop-in: the same type
+ * layouts, names, arguments and return values as the reference, so code that
+ * calls llama2.c's sampler links against libb200_sampler.so unchanged.  The
+ * computation runs on the current CUDA device; the host buffers keep their
+ * reference meaning (sample() overwrites `logits` with the probabilities when
+ * temperature != 0).
+ *
+ * Part 2 adds what the reference does not have: a batched device entry point
+ * over B independent rows with per-row xorshift state, the fused classifier
+ * GEMM + sampling entry point, and multi-GPU helpers (row sharding and an
+ * optional NCCL gather of the sampled ids).
+ *
+ * Reference citations are file:line within the reference project.
+ * All Part-2 functions return 0 on success or a negative SAMPLER_E* code and
+ * never exit the process.
+ */
+#ifndef B200_SAMPLER_H_
+#define B200_SAMPLER_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------
+ * Part 1: llama2.c Sampler surface
+ * ---------------------------------------------------------------------- */
+
+/* Replaces ProbIndex, llama2.c:968-971 (same 8-byte layout). */
+typedef struct {
+    float prob;
+    int index;
+} ProbIndex;
+
+/* Replaces Sampler, llama2.c:973-979 (same layout). */
+typedef struct {
+    int vocab_size;
+    ProbIndex* probindex; /* host scratch, allocated by build_sampler */
+    float temperature;
+    float topp;
+    unsigned long long rng_state;
+} Sampler;
+
+/* Replaces build_sampler, llama2.c:1058-1065. */
+void build_sampler(Sampler* sampler, int vocab_size, float temperature, float topp,
+                   unsigned long long rng_seed);
+/* Replaces free_sampler, llama2.c:1067-1069. */
+void free_sampler(Sampler* sampler);
+/* Replaces random_u32, llama2.c:1071-1077 (xorshift*, host integer math). */
+unsigned int random_u32(unsigned long long* state);
+/* Replaces random_f32, llama2.c:1078-1080. */
+float random_f32(unsigned long long* state);
+/* Replaces sample_argmax, llama2.c:981-992.  Host buffer, device compute. */
+int sample_argmax(float* probabilities, int n);
+/* Replaces sample_mult, llama2.c:994-1005.  Host buffer, device compute. */
+int sample_mult(float* probabilities, int n, float coin);
+/* Replaces sample_topp, llama2.c:1015-1056.  Host buffer, device compute.
+ * `probindex` is accepted for signature compatibility and left untouched
+ * (the reference uses it as sort scratch only). */
+int sample_topp(float* probabilities, int n, float topp, ProbIndex* probindex, float coin);
+/* Replaces sample, llama2.c:1082-1105.  `logits` is a host buffer of
+ * vocab_size floats; when temperature != 0 it is overwritten with the
+ * softmax probabilities and rng_state advances by one draw, as in the
+ * reference.  Returns the token id (or -1 if the device call failed; see
+ * sampler_last_error()). */
+int sample(Sampler* sampler, float* logits);
+
+/* ------------------------------------------------------------------------
+ * Part 2: batched device API (no counterpart in the reference; it extends
+ * the per-row sample() call above to B rows)
+ * ---------------------------------------------------------------------- */
+
+#define SAMPLER_OK 0
+#define SAMPLER_E_INVALID (-1)      /* bad argument (null pointer, size, alignment) */
+#define SAMPLER_E_UNSUPPORTED (-2)  /* vocab_size above the supported maximum */
+#define SAMPLER_E_CUDA (-3)         /* a CUDA runtime call failed */
+#define SAMPLER_E_WORKSPACE (-4)    /* caller workspace too small */
+#define SAMPLER_E_NCCL (-5)         /* NCCL missing or a NCCL call failed */
+#define SAMPLER_E_DEVICE (-6)       /* the device reported a bounded-wait timeout */
+
+/* Row flags written to row_flags[] (when non-NULL). */
+#define SAMPLER_ROW_NAN 1          /* NaN reached the softmax: probabilities are NaN */
+#define SAMPLER_ROW_NO_CANDIDATE 2 /* top-p found no candidate (reference reads probindex[-1]); id 0 */
+#define SAMPLER_ROW_SLOW_PATH 4    /* nucleus exceeded on-chip capacity; global-memory path used */
+#define SAMPLER_ROW_SERIAL 8       /* input not a non-negative finite distribution; serial replay */
+#define SAMPLER_ROW_TIMEOUT 16     /* a bounded device wait expired; result invalid */
+
+/* Flags for SamplerBatchConfig.flags */
+#define SAMPLER_FLAG_PROBS_IN 1 /* rows are probabilities: skip /T and softmax, go straight to
+                                   sample_mult / sample_topp (the coin is still drawn) */
+
+/* Largest vocabulary the on-chip row path supports (the row is staged whole
+ * in shared memory). */
+#define SAMPLER_MAX_VOCAB 32768
+
+typedef struct {
+    int vocab_size;    /* V, 2 <= V <= SAMPLER_MAX_VOCAB */
+    float temperature; /* used for every row unless temperature_rows != NULL */
+    float topp;        /* used for every row unless topp_rows != NULL */
+    int flags;         /* SAMPLER_FLAG_* */
+} SamplerBatchConfig;
+
+/* Bytes of device workspace sampler_batched needs for `batch` rows of
+ * `vocab_size` (the global-memory sort scratch of the slow top-p path). */
+size_t sampler_workspace_bytes(int batch, int vocab_size);
+
+/* Batched sampling of `batch` rows on the device (all pointers are device
+ * pointers; `stream` is a cudaStream_t or NULL for the default stream).
+ *   logits           [batch, ld] fp32, row r at logits + r*ld (read only)
+ *   temperature_rows [batch] or NULL (then cfg->temperature)
+ *   topp_rows        [batch] or NULL (then cfg->topp)
+ *   coins            [batch] or NULL: a given coin per row instead of a draw
+ *                    from rng_state (rng_state is then neither read nor written)
+ *   rng_state        [batch] xorshift states, advanced in place by one draw on
+ *                    rows with temperature != 0 (may be NULL when coins given
+ *                    or every row is greedy)
+ *   out_ids          [batch] int32 token ids
+ *   probs_out        [batch, vocab_size] or NULL: the probabilities sample()
+ *                    leaves in its buffer (softmax output; logits when greedy)
+ *   row_flags        [batch] or NULL: SAMPLER_ROW_* bits per row
+ *   workspace        NULL (library-managed) or >= sampler_workspace_bytes()
+ * Per row it follows sample() (llama2.c:1082-1105) exactly: greedy when
+ * temperature == 0, else /T, softmax, coin, then sample_mult when topp <= 0
+ * or topp >= 1, else sample_topp.  Asynchronous on `stream`. */
+int sampler_batched(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
+                    const float* temperature_rows, const float* topp_rows, const float* coins,
+                    unsigned long long* rng_state, int* out_ids, float* probs_out, int* row_flags,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same as sampler_batched but every buffer is a HOST buffer; copies to and
+ * from the device happen inside (pinned or pageable host memory).  Rows are
+ * pipelined in chunks over two streams so copies overlap sampling.
+ * rng_state (host) is advanced in place. */
+int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int batch,
+                         long long ld, const float* topp_rows, unsigned long long* rng_state,
+                         int* out_ids);
+
+/* rng_state[r] = rng_seed + row_offset + r for r < batch (device buffer):
+ * the per-row seeding rule of the batched API (row r of the global batch is
+ * seeded rng_seed + r). */
+int sampler_seed_states(unsigned long long* rng_state, int batch, unsigned long long rng_seed,
+                        long long row_offset, void* stream);
+
+/* Number of kernel launches the last sampler_batched call on this thread
+ * issued (diagnostic; used by the benchmark's launch count). */
+int sampler_last_launch_count(void);
+
+/* Human-readable text of the last error on this thread. */
+const char* sampler_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Multi-GPU helpers (no counterpart in the reference, which is single-GPU:
+ * llama2_cublas.cu:6065 calls cudaSetDevice(0)).
+ * ---------------------------------------------------------------------- */
+
+/* Contiguous row shard of rank `rank` out of `world` for a global batch:
+ * rows [*row_begin, *row_begin + *row_count). */
+int sampler_shard_rows(int batch, int world, int rank, int* row_begin, int* row_count);
+
+/* NCCL is loaded at run time (dlopen of libnccl.so.2); these return
+ * SAMPLER_E_NCCL when it is absent.  The id is NCCL's 128-byte unique id. */
+int sampler_nccl_get_unique_id(void* id128);
+int sampler_nccl_comm_init(void** comm, int nranks, const void* id128, int rank);
+/* All-gather of equal-sized int32 id shards (rows_per_rank each) into
+ * ids_all [nranks * rows_per_rank] on every rank; device buffers. */
+int sampler_nccl_allgather_ids(void* comm, const int* ids_local, int rows_per_rank, int* ids_all,
+                               void* stream);
+int sampler_nccl_comm_destroy(void* comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_SAMPLER_H_ */

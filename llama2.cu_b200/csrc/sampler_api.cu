@@ -1,0 +1,509 @@
+// sampler_api.cu -- host side of the C-ABI declared in include/b200_sampler.h.
+//
+// The llama2.c entry points keep the reference's meaning (llama2.c:964-1105)
+// and route the per-row work to the device kernels in sampler_kernels.cu.
+// There is no CPU implementation of the sampling arithmetic here: if the
+// device or the kernels are unavailable, calls fail (-1 / SAMPLER_E_*) with a
+// message in sampler_last_error().
+#include "../../include/b200_sampler.h"
+#include "sampler_kernels.cuh"
+
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int g_last_launches = 0;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define B2S_CUDA(call)                                                                      \
+    do {                                                                                    \
+        cudaError_t e_ = (call);                                                            \
+        if (e_ != cudaSuccess)                                                              \
+            return fail(SAMPLER_E_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));     \
+    } while (0)
+
+size_t next_pow2(size_t x) {
+    size_t p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+// Per-device state for the library-managed buffers.
+struct DeviceCtx {
+    int device = -1;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;   // used by the single-row llama2.c entry points
+    cudaStream_t streams[2] = {nullptr, nullptr};  // host-buffer pipeline
+    int* error_word = nullptr;
+    unsigned long long* workspace = nullptr;
+    size_t workspace_bytes = 0;
+    // single-row buffers
+    float* d_row = nullptr;
+    float* d_probs = nullptr;
+    float* d_coin = nullptr;
+    int* d_id = nullptr;
+    int row_cap = 0;
+    // host-pipeline buffers
+    float* d_logits = nullptr;
+    size_t logits_cap = 0;
+    float* d_topp = nullptr;
+    unsigned long long* d_state = nullptr;
+    int* d_ids = nullptr;
+    int rows_cap = 0;
+};
+
+std::mutex g_mu;
+std::vector<DeviceCtx*> g_ctx;
+
+int get_ctx(DeviceCtx** out) {
+    int dev = 0;
+    B2S_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_mu);
+    if ((int)g_ctx.size() <= dev) g_ctx.resize(dev + 1, nullptr);
+    if (!g_ctx[dev]) {
+        DeviceCtx* c = new DeviceCtx();
+        c->device = dev;
+        B2S_CUDA(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, dev));
+        B2S_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+        B2S_CUDA(cudaStreamCreateWithFlags(&c->streams[0], cudaStreamNonBlocking));
+        B2S_CUDA(cudaStreamCreateWithFlags(&c->streams[1], cudaStreamNonBlocking));
+        B2S_CUDA(cudaMalloc(&c->error_word, sizeof(int)));
+        B2S_CUDA(cudaMemset(c->error_word, 0, sizeof(int)));
+        B2S_CUDA(cudaMalloc(&c->d_coin, 4 * sizeof(float)));
+        B2S_CUDA(cudaMalloc(&c->d_id, 4 * sizeof(int)));
+        g_ctx[dev] = c;
+    }
+    *out = g_ctx[dev];
+    return SAMPLER_OK;
+}
+
+int ensure_workspace(DeviceCtx* c, size_t bytes) {
+    if (c->workspace_bytes >= bytes) return SAMPLER_OK;
+    if (c->workspace) cudaFree(c->workspace);
+    c->workspace = nullptr;
+    c->workspace_bytes = 0;
+    B2S_CUDA(cudaMalloc(&c->workspace, bytes));
+    c->workspace_bytes = bytes;
+    return SAMPLER_OK;
+}
+
+int ensure_row(DeviceCtx* c, int V) {
+    if (c->row_cap >= V) return SAMPLER_OK;
+    if (c->d_row) cudaFree(c->d_row);
+    if (c->d_probs) cudaFree(c->d_probs);
+    c->d_row = c->d_probs = nullptr;
+    c->row_cap = 0;
+    B2S_CUDA(cudaMalloc(&c->d_row, (size_t)V * sizeof(float)));
+    B2S_CUDA(cudaMalloc(&c->d_probs, (size_t)V * sizeof(float)));
+    c->row_cap = V;
+    return SAMPLER_OK;
+}
+
+int row_ctas(const DeviceCtx* c, int batch) { return batch < c->num_sms ? batch : c->num_sms; }
+
+size_t workspace_for(int ctas, int V) { return (size_t)ctas * next_pow2((size_t)V) * sizeof(unsigned long long); }
+
+// Core dispatcher shared by every entry point.  All pointers are device
+// pointers.  force_mode: 0 = sample() dispatch by topp, 1 = sample_mult,
+// 2 = sample_topp.
+int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
+             const float* temperature_rows, const float* topp_rows, const float* coins,
+             unsigned long long* rng_state, int* out_ids, float* probs_out, int* row_flags,
+             void* workspace, size_t workspace_bytes, cudaStream_t stream, int force_mode) {
+    g_last_launches = 0;
+    if (!cfg || !logits || !out_ids) return fail(SAMPLER_E_INVALID, "null config, logits or out_ids");
+    const int V = cfg->vocab_size;
+    if (batch < 0 || V < 1 || ld < V) return fail(SAMPLER_E_INVALID, "bad sizes: batch=%d vocab=%d ld=%lld", batch, V, ld);
+    if (V > SAMPLER_MAX_VOCAB)
+        return fail(SAMPLER_E_UNSUPPORTED, "vocab_size %d above SAMPLER_MAX_VOCAB %d", V, SAMPLER_MAX_VOCAB);
+    if (batch == 0) return SAMPLER_OK;
+    const bool probs_in = (cfg->flags & SAMPLER_FLAG_PROBS_IN) != 0;
+    const bool all_greedy = !probs_in && !temperature_rows && cfg->temperature == 0.0f && force_mode == 0;
+    if (!all_greedy && !coins && !rng_state)
+        return fail(SAMPLER_E_INVALID, "rng_state is NULL but rows need a coin");
+    DeviceCtx* c = nullptr;
+    int rc = get_ctx(&c);
+    if (rc) return rc;
+
+    if (all_greedy) {
+        b2s::ArgmaxLaunch a{logits, ld, batch, V, out_ids, probs_out};
+        const int n = b2s::launch_argmax(a, stream);
+        if (n < 0) return fail(SAMPLER_E_CUDA, "argmax launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+        if (row_flags) B2S_CUDA(cudaMemsetAsync(row_flags, 0, (size_t)batch * sizeof(int), stream));
+        g_last_launches = n + (row_flags ? 1 : 0);
+        return SAMPLER_OK;
+    }
+
+    const int ctas = row_ctas(c, batch);
+    const size_t need = workspace_for(ctas, V);
+    unsigned long long* ws = nullptr;
+    if (workspace) {
+        if (workspace_bytes < need)
+            return fail(SAMPLER_E_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
+        if (((uintptr_t)workspace & 15u) != 0) return fail(SAMPLER_E_INVALID, "workspace not 16-byte aligned");
+        ws = static_cast<unsigned long long*>(workspace);
+    } else {
+        std::lock_guard<std::mutex> lk(g_mu);
+        rc = ensure_workspace(c, need);
+        if (rc) return rc;
+        ws = c->workspace;
+    }
+    b2s::RowLaunch p{};
+    p.logits = logits;
+    p.ld = ld;
+    p.batch = batch;
+    p.vocab = V;
+    p.temperature = cfg->temperature;
+    p.topp = cfg->topp;
+    p.temperature_rows = temperature_rows;
+    p.topp_rows = topp_rows;
+    p.coins = coins;
+    p.rng_state = rng_state;
+    p.out_ids = out_ids;
+    p.probs_out = probs_out;
+    p.row_flags = row_flags;
+    p.workspace = ws;
+    p.ws_stride = (long long)next_pow2((size_t)V);
+    p.probs_in = probs_in ? 1 : 0;
+    p.force_mode = force_mode;
+    p.error_word = c->error_word;
+    const int n = b2s::launch_row_sampler(p, ctas, stream);
+    if (n < 0) return fail(SAMPLER_E_CUDA, "row sampler launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+    g_last_launches = n;
+    return SAMPLER_OK;
+}
+
+// Reads and clears the device error word after a synchronize.
+int check_device_word(DeviceCtx* c) {
+    int w = 0;
+    B2S_CUDA(cudaMemcpy(&w, c->error_word, sizeof(int), cudaMemcpyDeviceToHost));
+    if (w) {
+        B2S_CUDA(cudaMemset(c->error_word, 0, sizeof(int)));
+        return fail(SAMPLER_E_DEVICE, "a bounded device wait expired");
+    }
+    return SAMPLER_OK;
+}
+
+// One host row through the device: the shared body of the llama2.c
+// single-row entry points.  Returns the id or -1.
+int host_row(float* row, int n, float temperature, float topp, const float* coin, int probs_in,
+             int force_mode, bool write_back) {
+    DeviceCtx* c = nullptr;
+    if (get_ctx(&c)) return -1;
+    if (n < 1 || n > SAMPLER_MAX_VOCAB) {
+        fail(SAMPLER_E_UNSUPPORTED, "vocab_size %d outside [1, %d]", n, SAMPLER_MAX_VOCAB);
+        return -1;
+    }
+    if (ensure_row(c, n)) return -1;
+    cudaStream_t s = c->stream;
+    if (cudaMemcpyAsync(c->d_row, row, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        fail(SAMPLER_E_CUDA, "H2D copy failed");
+        return -1;
+    }
+    if (coin && cudaMemcpyAsync(c->d_coin, coin, sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        fail(SAMPLER_E_CUDA, "H2D coin copy failed");
+        return -1;
+    }
+    SamplerBatchConfig cfg{n, temperature, topp, probs_in ? SAMPLER_FLAG_PROBS_IN : 0};
+    const int rc = dispatch(&cfg, c->d_row, 1, n, nullptr, nullptr, coin ? c->d_coin : nullptr, nullptr, c->d_id,
+                            write_back ? c->d_probs : nullptr, nullptr, nullptr, 0, s, force_mode);
+    if (rc) return -1;
+    int id = -1;
+    if (cudaMemcpyAsync(&id, c->d_id, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+        fail(SAMPLER_E_CUDA, "D2H id copy failed");
+        return -1;
+    }
+    if (write_back &&
+        cudaMemcpyAsync(row, c->d_probs, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+        fail(SAMPLER_E_CUDA, "D2H probabilities copy failed");
+        return -1;
+    }
+    if (cudaStreamSynchronize(s) != cudaSuccess) {
+        fail(SAMPLER_E_CUDA, "stream synchronize failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    if (check_device_word(c)) return -1;
+    return id;
+}
+
+// ---------------------------------------------------------------------------
+// NCCL, loaded at run time
+// ---------------------------------------------------------------------------
+struct NcclApi {
+    bool tried = false;
+    void* lib = nullptr;
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclCommDestroy) comm_destroy = nullptr;
+    decltype(&ncclGetErrorString) error_string = nullptr;
+};
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+
+int nccl_load() {
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    if (g_nccl.lib) return SAMPLER_OK;
+    if (g_nccl.tried) return fail(SAMPLER_E_NCCL, "libnccl.so.2 could not be loaded");
+    g_nccl.tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return fail(SAMPLER_E_NCCL, "dlopen libnccl.so.2: %s", dlerror());
+    g_nccl.get_unique_id = (decltype(&ncclGetUniqueId))dlsym(h, "ncclGetUniqueId");
+    g_nccl.comm_init_rank = (decltype(&ncclCommInitRank))dlsym(h, "ncclCommInitRank");
+    g_nccl.all_gather = (decltype(&ncclAllGather))dlsym(h, "ncclAllGather");
+    g_nccl.comm_destroy = (decltype(&ncclCommDestroy))dlsym(h, "ncclCommDestroy");
+    g_nccl.error_string = (decltype(&ncclGetErrorString))dlsym(h, "ncclGetErrorString");
+    if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.all_gather || !g_nccl.comm_destroy)
+        return fail(SAMPLER_E_NCCL, "libnccl.so.2 lacks a required symbol");
+    g_nccl.lib = h;
+    return SAMPLER_OK;
+}
+
+int nccl_fail(ncclResult_t r, const char* what) {
+    return fail(SAMPLER_E_NCCL, "%s: %s", what, g_nccl.error_string ? g_nccl.error_string(r) : "nccl error");
+}
+
+}  // namespace
+
+// ===========================================================================
+// Part 1: llama2.c Sampler surface
+// ===========================================================================
+extern "C" {
+
+void build_sampler(Sampler* sampler, int vocab_size, float temperature, float topp,
+                   unsigned long long rng_seed) {
+    sampler->vocab_size = vocab_size;
+    sampler->temperature = temperature;
+    sampler->topp = topp;
+    sampler->rng_state = rng_seed;
+    // host scratch with the reference's size (llama2.c:1064); the device path
+    // does not need it but callers may rely on it existing
+    sampler->probindex = (ProbIndex*)malloc((size_t)vocab_size * sizeof(ProbIndex));
+}
+
+void free_sampler(Sampler* sampler) {
+    free(sampler->probindex);
+    sampler->probindex = nullptr;
+}
+
+unsigned int random_u32(unsigned long long* state) {
+    unsigned long long s = *state;
+    s ^= s >> 12;
+    s ^= s << 25;
+    s ^= s >> 27;
+    *state = s;
+    return (unsigned int)((s * 0x2545F4914F6CDD1Dull) >> 32);
+}
+
+float random_f32(unsigned long long* state) { return (random_u32(state) >> 8) / 16777216.0f; }
+
+int sample_argmax(float* probabilities, int n) {
+    return host_row(probabilities, n, 0.0f, 0.0f, nullptr, 0, 0, false);
+}
+
+int sample_mult(float* probabilities, int n, float coin) {
+    return host_row(probabilities, n, 1.0f, 1.0f, &coin, 1, 1, false);
+}
+
+int sample_topp(float* probabilities, int n, float topp, ProbIndex* probindex, float coin) {
+    (void)probindex;
+    return host_row(probabilities, n, 1.0f, topp, &coin, 1, 2, false);
+}
+
+int sample(Sampler* sampler, float* logits) {
+    if (sampler->temperature == 0.0f)
+        return host_row(logits, sampler->vocab_size, 0.0f, sampler->topp, nullptr, 0, 0, false);
+    // The coin comes from the Sampler's own state exactly as llama2.c:1094
+    // draws it (host integer arithmetic), then the device does the rest.
+    const float coin = random_f32(&sampler->rng_state);
+    return host_row(logits, sampler->vocab_size, sampler->temperature, sampler->topp, &coin, 0, 0, true);
+}
+
+// ===========================================================================
+// Part 2: batched API
+// ===========================================================================
+size_t sampler_workspace_bytes(int batch, int vocab_size) {
+    DeviceCtx* c = nullptr;
+    int sms = 148;
+    if (get_ctx(&c) == SAMPLER_OK) sms = c->num_sms;
+    const int ctas = batch < sms ? (batch < 1 ? 1 : batch) : sms;
+    return workspace_for(ctas, vocab_size < 1 ? 1 : vocab_size);
+}
+
+int sampler_batched(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
+                    const float* temperature_rows, const float* topp_rows, const float* coins,
+                    unsigned long long* rng_state, int* out_ids, float* probs_out, int* row_flags,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+    return dispatch(cfg, logits, batch, ld, temperature_rows, topp_rows, coins, rng_state, out_ids, probs_out,
+                    row_flags, workspace, workspace_bytes, (cudaStream_t)stream, 0);
+}
+
+int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
+                         const float* topp_rows, unsigned long long* rng_state, int* out_ids) {
+    g_last_launches = 0;
+    if (!cfg || !logits || !out_ids) return fail(SAMPLER_E_INVALID, "null config, logits or out_ids");
+    const int V = cfg->vocab_size;
+    if (batch < 0 || V < 1 || ld < V) return fail(SAMPLER_E_INVALID, "bad sizes");
+    if (batch == 0) return SAMPLER_OK;
+    DeviceCtx* c = nullptr;
+    int rc = get_ctx(&c);
+    if (rc) return rc;
+    const bool all_greedy = !(cfg->flags & SAMPLER_FLAG_PROBS_IN) && cfg->temperature == 0.0f;
+    if (!all_greedy && !rng_state) return fail(SAMPLER_E_INVALID, "rng_state is NULL");
+    // Each of the two pipeline streams gets its own half of the workspace so
+    // two chunks in flight never share slow-path scratch.
+    const size_t ws_half = workspace_for(row_ctas(c, batch), V);
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        rc = ensure_workspace(c, 2 * ws_half);
+        if (rc) return rc;
+        const size_t need = (size_t)batch * (size_t)V;
+        if (c->logits_cap < need) {
+            if (c->d_logits) cudaFree(c->d_logits);
+            c->d_logits = nullptr;
+            c->logits_cap = 0;
+            B2S_CUDA(cudaMalloc(&c->d_logits, need * sizeof(float)));
+            c->logits_cap = need;
+        }
+        if (c->rows_cap < batch) {
+            if (c->d_topp) cudaFree(c->d_topp);
+            if (c->d_state) cudaFree(c->d_state);
+            if (c->d_ids) cudaFree(c->d_ids);
+            c->d_topp = nullptr;
+            c->d_state = nullptr;
+            c->d_ids = nullptr;
+            c->rows_cap = 0;
+            B2S_CUDA(cudaMalloc(&c->d_topp, (size_t)batch * sizeof(float)));
+            B2S_CUDA(cudaMalloc(&c->d_state, (size_t)batch * sizeof(unsigned long long)));
+            B2S_CUDA(cudaMalloc(&c->d_ids, (size_t)batch * sizeof(int)));
+            c->rows_cap = batch;
+        }
+    }
+    // Chunks of rows alternate between two streams: the copy of chunk k+1
+    // overlaps the sampling of chunk k.
+    int chunk = (batch + 7) / 8;  // about eight chunks, each at least one CTA per SM
+    if (chunk < c->num_sms) chunk = batch < c->num_sms ? batch : c->num_sms;
+    int launches = 0;
+    for (int r0 = 0, k = 0; r0 < batch; r0 += chunk, ++k) {
+        const int rows = (batch - r0) < chunk ? (batch - r0) : chunk;
+        cudaStream_t s = c->streams[k & 1];
+        float* dl = c->d_logits + (size_t)r0 * V;
+        if (ld == V) {
+            B2S_CUDA(cudaMemcpyAsync(dl, logits + (size_t)r0 * V, (size_t)rows * V * sizeof(float),
+                                     cudaMemcpyHostToDevice, s));
+        } else {
+            B2S_CUDA(cudaMemcpy2DAsync(dl, (size_t)V * sizeof(float), logits + (size_t)r0 * ld,
+                                       (size_t)ld * sizeof(float), (size_t)V * sizeof(float), rows,
+                                       cudaMemcpyHostToDevice, s));
+        }
+        if (topp_rows)
+            B2S_CUDA(cudaMemcpyAsync(c->d_topp + r0, topp_rows + r0, rows * sizeof(float), cudaMemcpyHostToDevice, s));
+        if (!all_greedy)
+            B2S_CUDA(cudaMemcpyAsync(c->d_state + r0, rng_state + r0, rows * sizeof(unsigned long long),
+                                     cudaMemcpyHostToDevice, s));
+        void* ws = reinterpret_cast<char*>(c->workspace) + (size_t)(k & 1) * ws_half;
+        rc = dispatch(cfg, dl, rows, V, nullptr, topp_rows ? c->d_topp + r0 : nullptr, nullptr,
+                      all_greedy ? nullptr : c->d_state + r0, c->d_ids + r0, nullptr, nullptr, ws, ws_half, s, 0);
+        if (rc) return rc;
+        launches += g_last_launches;
+        B2S_CUDA(cudaMemcpyAsync(out_ids + r0, c->d_ids + r0, rows * sizeof(int), cudaMemcpyDeviceToHost, s));
+        if (!all_greedy)
+            B2S_CUDA(cudaMemcpyAsync(rng_state + r0, c->d_state + r0, rows * sizeof(unsigned long long),
+                                     cudaMemcpyDeviceToHost, s));
+    }
+    B2S_CUDA(cudaStreamSynchronize(c->streams[0]));
+    B2S_CUDA(cudaStreamSynchronize(c->streams[1]));
+    g_last_launches = launches;
+    return check_device_word(c);
+}
+
+int sampler_seed_states(unsigned long long* rng_state, int batch, unsigned long long rng_seed,
+                        long long row_offset, void* stream) {
+    if (!rng_state || batch < 0) return fail(SAMPLER_E_INVALID, "bad arguments");
+    if (batch == 0) return SAMPLER_OK;
+    const int n = b2s::launch_seed_states(rng_state, batch, rng_seed, row_offset, (cudaStream_t)stream);
+    if (n < 0) return fail(SAMPLER_E_CUDA, "seed launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+    return SAMPLER_OK;
+}
+
+int sampler_last_launch_count(void) { return g_last_launches; }
+
+const char* sampler_last_error(void) { return g_last_error.c_str(); }
+
+// ===========================================================================
+// Multi-GPU helpers
+// ===========================================================================
+int sampler_shard_rows(int batch, int world, int rank, int* row_begin, int* row_count) {
+    if (batch < 0 || world < 1 || rank < 0 || rank >= world || !row_begin || !row_count)
+        return fail(SAMPLER_E_INVALID, "bad shard arguments");
+    const int base = batch / world, rem = batch % world;
+    *row_begin = rank * base + (rank < rem ? rank : rem);
+    *row_count = base + (rank < rem ? 1 : 0);
+    return SAMPLER_OK;
+}
+
+int sampler_nccl_get_unique_id(void* id128) {
+    if (!id128) return fail(SAMPLER_E_INVALID, "null id buffer");
+    int rc = nccl_load();
+    if (rc) return rc;
+    ncclUniqueId id;
+    const ncclResult_t r = g_nccl.get_unique_id(&id);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+    memcpy(id128, &id, sizeof(id));
+    return SAMPLER_OK;
+}
+
+int sampler_nccl_comm_init(void** comm, int nranks, const void* id128, int rank) {
+    if (!comm || !id128) return fail(SAMPLER_E_INVALID, "null argument");
+    int rc = nccl_load();
+    if (rc) return rc;
+    ncclUniqueId id;
+    memcpy(&id, id128, sizeof(id));
+    ncclComm_t cm = nullptr;
+    const ncclResult_t r = g_nccl.comm_init_rank(&cm, nranks, id, rank);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
+    *comm = cm;
+    return SAMPLER_OK;
+}
+
+int sampler_nccl_allgather_ids(void* comm, const int* ids_local, int rows_per_rank, int* ids_all, void* stream) {
+    if (!comm || !ids_local || !ids_all || rows_per_rank < 0) return fail(SAMPLER_E_INVALID, "bad arguments");
+    int rc = nccl_load();
+    if (rc) return rc;
+    const ncclResult_t r = g_nccl.all_gather(ids_local, ids_all, (size_t)rows_per_rank, ncclInt32,
+                                             (ncclComm_t)comm, (cudaStream_t)stream);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+    return SAMPLER_OK;
+}
+
+int sampler_nccl_comm_destroy(void* comm) {
+    if (!comm) return SAMPLER_OK;
+    int rc = nccl_load();
+    if (rc) return rc;
+    const ncclResult_t r = g_nccl.comm_destroy((ncclComm_t)comm);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclCommDestroy");
+    return SAMPLER_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,51 @@
+// sampler_kernels.cuh -- launch interface between the C-ABI host code and the
+// device kernels of the logits -> token path.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b2s {
+
+constexpr int kRowThreads = 1024;      // threads of the row kernel (one CTA per SM)
+constexpr int kRowCPT = 32;            // row elements per thread chunk
+constexpr int kRowCap = kRowThreads * kRowCPT;  // 32768 floats staged on chip
+constexpr int kCandCap = 8192;         // nucleus candidates kept on chip
+
+struct RowLaunch {
+    const float* logits;  // [B, ld]
+    long long ld;
+    int batch;
+    int vocab;
+    float temperature;            // when temperature_rows == nullptr
+    float topp;                   // when topp_rows == nullptr
+    const float* temperature_rows;
+    const float* topp_rows;
+    const float* coins;           // optional given coins
+    unsigned long long* rng_state;
+    int* out_ids;
+    float* probs_out;             // optional [B, vocab]
+    int* row_flags;               // optional [B]
+    unsigned long long* workspace;  // per-CTA slow-path scratch
+    long long ws_stride;          // u64 entries per CTA (power of two >= vocab)
+    int probs_in;                 // rows are probabilities
+    int force_mode;               // 0: by topp as sample() does, 1: sample_mult, 2: sample_topp
+    int* error_word;              // device word, set on bounded-wait timeout
+};
+
+struct ArgmaxLaunch {
+    const float* logits;
+    long long ld;
+    int batch;
+    int vocab;
+    int* out_ids;
+    float* probs_out;  // optional copy of the rows (sample() leaves logits untouched)
+};
+
+// Returns the number of kernels launched (>= 1) or a negative cudaError_t.
+int launch_row_sampler(const RowLaunch& p, int num_ctas, cudaStream_t stream);
+int launch_argmax(const ArgmaxLaunch& p, cudaStream_t stream);
+int launch_seed_states(unsigned long long* st, int batch, unsigned long long seed,
+                       long long offset, cudaStream_t stream);
+size_t row_kernel_smem_bytes();
+
+}  // namespace b2s
