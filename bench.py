@@ -267,7 +267,7 @@ def run_ours(args):
                                 l2="inputs 524 MB per GPU > 126 MB L2; no flush"),
                     hbm_gbs=world * alg_bytes / (ms * 1e-3) / 1e9,
                     roofline=dict(bound="hbm", achieved=achieved, peak=peak, unit="GB/s", frac=achieved / peak,
-                                  traffic=traffic, kernel="row_sampler_kernel", kernel_ms=kernel_ms,
+                                  traffic=traffic, kernel="row_stream_kernel", kernel_ms=kernel_ms,
                                   peak_source=peak_note),
                     cpu_baseline=cpu,
                     e2e=dict(value=world * B / (e2e_ms * 1e-3), unit="tokens/s",

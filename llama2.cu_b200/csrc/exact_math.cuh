@@ -101,9 +101,20 @@ XM_HD float exp_normal_range(float d, const ExpTableEntry* tab) {
 constexpr float kExpFastMin = -87.0f;  // ln(2^-126) = -87.3365...
 constexpr float kExpFastMax = 88.0f;   // ln(FLT_MAX) = 88.7228...
 
+// The rare out-of-range path, kept out of line so the unrolled callers do
+// not carry its register footprint.
+#if defined(__CUDACC__)
+static __host__ __device__ __noinline__
+#else
+static inline
+#endif
+float exp_outside_fast_range(float d) {
+    return (float)exp((double)d);
+}
+
 XM_HD float exp_f32(float d, const ExpTableEntry* tab) {
     if (d >= kExpFastMin && d <= kExpFastMax) return exp_normal_range(d, tab);
-    return (float)exp((double)d);
+    return exp_outside_fast_range(d);
 }
 
 // The 2^(j/N) table entry j as an fp32 hi/lo pair, from double-precision exp2.
@@ -197,6 +208,28 @@ XM_HD uint32_t chain_guess_binade(float g, float sigma) {
     // guess costs speed only: chain_apply rejects it and the chunk replays.
     if (!(g >= XM_MUL(lo, 1.0009765625f))) return 0u;
     if (!(XM_ADD(g, sigma) <= XM_MUL(hi, 0.9990234375f))) return 0u;
+    return eb;
+}
+
+
+// Binade the running sum of a chunk is expected to sit in, from an
+// approximate incoming value g: binade(g), or 0 when g is zero or below
+// 2^-100 (such chunks are replayed).  `alt` receives the neighbouring binade
+// the exact serial sum may fall into instead -- when g, or the chunk's end
+// g + sigma, lies within 2^-10 of a binade boundary -- or 0.  The caller
+// builds chunk functions for both, and the resolution picks whichever
+// matches the exact running sum.
+XM_HD uint32_t chain_guess_primary(float g, float sigma, uint32_t& alt) {
+    alt = 0u;
+    const uint32_t eb = binade_of(g);
+    if (!(g > 0.0f) || eb < kMinFastBinade || eb >= 253u) return 0u;
+    const float lo = XM_U2F(eb << 23);
+    const float hi = XM_U2F((eb + 1u) << 23);
+    if (!(g >= XM_MUL(lo, 1.0009765625f))) {
+        if (eb - 1u >= kMinFastBinade) alt = eb - 1u;
+    } else if (!(XM_ADD(g, sigma) <= XM_MUL(hi, 0.9990234375f))) {
+        alt = eb + 1u;
+    }
     return eb;
 }
 

@@ -1,0 +1,811 @@
+// row_stream.cu -- the streaming top-p kernel (the fast path for sample()).
+//
+// Four 256-thread CTAs per SM, each owning one row at a time (persistent
+// grid).  While one CTA is in a sequential phase (the exact serial-sum
+// resolution, the nucleus walk), the other CTAs on the SM keep its pipes and
+// the HBM busy.  The row (V <= 32768) is walked in four strips of 8192
+// elements; in strip s thread t owns the 32-element chunk 256s + t, loaded
+// with eight independent 16-byte loads.
+//
+//   Pass 1 (HBM read): max/min of the logits and, per chunk, an approximate
+//     online sum of exp(x - max) (ex2.approx) -- only used to guess which
+//     binade the serial running sum sits in at every chunk.
+//   Pass 2 (the same bytes, now in L2): x = l/T (Markstein division) and
+//     d = x - max.  An element whose e = exp(d) is provably below half an ulp
+//     of the (guessed) running sum is absorbed by the serial fp32 sum --
+//     llama2.c's loop adds it and nothing changes -- so its exact e is never
+//     needed: e = 0 stands in for it.  Everything else gets the exact
+//     table-driven exp.  The binade-chain function of the chunk is built on
+//     the fly (exact_math.cuh), plus an alternative for the neighbouring
+//     binade when the guess lies near a boundary.  Top-p candidates
+//     (e >= cutoff*S, with margin) go to an L2-resident per-CTA list and a
+//     histogram over the top bits of e.
+//   Resolution (one warp): chunk functions -> the exact serial softmax
+//     denominator S; chunks that straddle a binade are replayed by a
+//     warp-cooperative exact chain.
+//   Nucleus: the smallest prefix of histogram bins whose guaranteed mass
+//     exceeds topp plus the fp32 drift bound is scattered on chip in bin
+//     order, each bin sorted by (e desc, index asc), p = fl(e/S), equal-p runs
+//     put in index order (glibc qsort's order), and the warp-cooperative
+//     chain walks the serial cumulative sum to topp and then to r = coin*cum.
+// Rows this kernel does not finish (sample_mult rows, nuclei above the
+// on-chip capacity, failed guesses without stored values) are appended to
+// the deferred-row list that the general row kernel processes next.
+#include "device_common.cuh"
+#include "exact_math.cuh"
+#include "sampler_kernels.cuh"
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+namespace b2s {
+namespace {
+
+constexpr int kST = 256;       // threads per CTA
+constexpr int kSW = kST / 32;  // warps per CTA
+constexpr int kSC = 32;        // elements per chunk
+constexpr int kStrips = 4;     // chunks per thread (strip s: chunk 256s + t)
+constexpr int kChunks = kST * kStrips;      // 1024 chunks of 32 (V <= 32768)
+constexpr int kSegs = kChunks / 32;         // 32 segments of 32 chunks
+constexpr int kKCap = 2048;    // nucleus keys kept on chip (more spill to L2)
+constexpr int kSideCap = 48;   // chunks whose values are kept for replays
+constexpr int kAltCap = 96;    // chunks with an alternative-binade function
+constexpr int kBinsPerThread = kBins / kST;  // 8
+
+// chunk entry: x=L0 y=L1 z=bits(pbits | flags | alt<<8 | side<<16) w=bits(eb)
+constexpr uint32_t kFClean = 4u, kFValid = 8u, kFAlt = 16u;
+
+struct StreamSmem {
+    unsigned long long kbuf[kKCap];
+    int hist[kBins];
+    short bstart[kBins];
+    float side[kSideCap][kSC];
+    float4 fn[kChunks];
+    float4 alt[kAltCap];
+    float4 wfn[kSegs];
+    xm::ExpTableEntry exptab[xm::kExpTableSize];
+    float red_a[kSW];
+    float red_b[kSW];
+    float red_c[kSW];
+    float red_s[kStrips][kSW];
+    int red_i[kSW];
+    int n_super;
+    int n_alt;
+    int n_side;
+    int flag;
+    int dbin;
+    int ksel;
+    int result;
+    float fval;
+};
+
+struct Ctx {
+    const float* src;  // row
+    int V;
+    int nch;
+    float T, rT;
+    float max_x;
+    bool unit;
+};
+
+// ---------------------------------------------------------------------------
+// block helpers (256 threads)
+// ---------------------------------------------------------------------------
+struct ScanF {
+    float incl, excl, total;
+};
+
+// Float scan whose exclusive value of thread t+1 is bitwise the inclusive
+// value of thread t, so "excl < x <= incl" selects exactly one thread.
+__device__ ScanF block_scan_f(float v, StreamSmem& sm) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(kFullMask, v, o);
+        if (lane >= o) v += y;
+    }
+    const float e = __shfl_up_sync(kFullMask, v, 1);
+    if (lane == 31) sm.red_a[warp] = v;
+    __syncthreads();
+    float p = 0.0f, t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kSW; ++w) {
+        const float x = sm.red_a[w];
+        if (w < warp) p += x;
+        t += x;
+    }
+    __syncthreads();
+    ScanF r;
+    r.incl = p + v;
+    r.excl = lane == 0 ? p : p + e;
+    r.total = t;
+    return r;
+}
+
+__device__ int block_scan_i(int v, StreamSmem& sm, int& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFullMask, v, o);
+        if (lane >= o) v += y;
+    }
+    if (lane == 31) sm.red_i[warp] = v;
+    __syncthreads();
+    int p = 0, t = 0;
+#pragma unroll
+    for (int w = 0; w < kSW; ++w) {
+        const int x = sm.red_i[w];
+        if (w < warp) p += x;
+        t += x;
+    }
+    __syncthreads();
+    total = t;
+    return p + v;
+}
+
+__device__ __forceinline__ xm::ChainFn fn_shfl_up(const xm::ChainFn& f, int o) {
+    return xm::ChainFn{__shfl_up_sync(kFullMask, f.L0, o), __shfl_up_sync(kFullMask, f.L1, o),
+                       __shfl_up_sync(kFullMask, f.pbits, o)};
+}
+__device__ __forceinline__ xm::ChainFn warp_incl_compose(xm::ChainFn f) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const xm::ChainFn y = fn_shfl_up(f, o);
+        if (lane >= o) f = xm::chain_compose(y, f);
+    }
+    return f;
+}
+
+// 2^x by the hardware approximation (only used for binade guesses).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ bool regular_sum(float s) {
+    const uint32_t eb = xm::binade_of(s);
+    return s > 0.0f && eb >= xm::kMinFastBinade && eb < 254u;
+}
+
+// ---------------------------------------------------------------------------
+// Warp-cooperative exact serial sum: s_i = fl(s_{i-1} + a_i) over i < n,
+// starting from the exact value s.  Returns the first i with s_i > theta
+// (s = s_i), or n (s = s_{n-1}).  While s is a normal number well above
+// 2^-100, 32 addends are handled per step: each lane forms its addend's
+// chain function in the binade of s, an inclusive warp scan composes them,
+// and every lane whose running sum stays in that binade is exact; the addend
+// that leaves the binade is added for real.  Addends must be >= 0.
+// ---------------------------------------------------------------------------
+template <class Get>
+__device__ int warp_chain(const Get& get, int n, float& s, float theta) {
+    const int lane = threadIdx.x & 31;
+    int pos = 0;
+    while (pos < n) {
+        const int i = pos + lane;
+        const float x = (i < n) ? get(i) : 0.0f;
+        if (regular_sum(s)) {
+            const uint32_t sb = __float_as_uint(s);
+            const uint32_t eb = (sb >> 23) & 0xFFu;
+            const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
+            const float v0 = __fadd_rn(lo, x), v1 = __fadd_rn(lo1, x);
+            const bool ok = (i < n) && ((__float_as_uint(v0) >> 23) == eb) && ((__float_as_uint(v1) >> 23) == eb);
+            xm::ChainFn f = ok ? xm::ChainFn{__fsub_rn(v0, lo), __fsub_rn(v1, lo1),
+                                             (__float_as_uint(v0) & 1u) | ((__float_as_uint(v1) & 1u) << 1)}
+                               : xm::chain_identity();
+            const unsigned okm = __ballot_sync(kFullMask, ok);
+            const int fi = (~okm) ? (__ffs(~okm) - 1) : 32;
+            f = warp_incl_compose(f);
+            const float hi = __uint_as_float((eb + 1u) << 23);
+            const float L = (sb & 1u) ? f.L1 : f.L0;
+            const bool inb = (lane < fi) && (L <= __fsub_rn(hi, s));
+            const unsigned inm = __ballot_sync(kFullMask, inb);
+            const int m = (~inm) ? (__ffs(~inm) - 1) : 32;
+            const float sl = __fadd_rn(s, L);
+            const unsigned hit = __ballot_sync(kFullMask, (lane < m) && (sl > theta));
+            if (hit) {
+                const int h = __ffs(hit) - 1;
+                s = __shfl_sync(kFullMask, sl, h);
+                return pos + h;
+            }
+            if (m > 0) s = __shfl_sync(kFullMask, sl, m - 1);
+            const float a = __shfl_sync(kFullMask, x, m & 31);
+            pos += m;
+            if (m < 32 && pos < n) {
+                s = __fadd_rn(s, a);
+                if (s > theta) return pos;
+                pos += 1;
+            }
+        } else if (s == 0.0f) {
+            const unsigned nz = __ballot_sync(kFullMask, (i < n) && (x != 0.0f));
+            if (!nz) {
+                pos += 32;
+                continue;
+            }
+            const int z = __ffs(nz) - 1;
+            const float a = __shfl_sync(kFullMask, x, z);
+            pos += z;
+            s = __fadd_rn(s, a);
+            if (s > theta) return pos;
+            pos += 1;
+        } else {
+            const float a = __shfl_sync(kFullMask, x, 0);
+            s = __fadd_rn(s, a);
+            if (s > theta) return pos;
+            pos += 1;
+        }
+    }
+    return n;
+}
+
+// Exact e value of one logit.
+__device__ __forceinline__ float exact_e(const Ctx& c, const StreamSmem& sm, float l) {
+    const float x = c.unit ? l : xm_div_const(l, c.T, c.rT);
+    return xm::exp_f32(__fsub_rn(x, c.max_x), sm.exptab);
+}
+
+// Replays chunk t exactly starting from s (warp 0): kept values, or values
+// recomputed from the row (no absorption) into the warp's scratch.
+__device__ float replay_chunk(StreamSmem& sm, const Ctx& c, int t, uint32_t side_plus1, float s) {
+    const int lane = threadIdx.x & 31;
+    const int base = t * kSC;
+    const int cnt = min(kSC, c.V - base);
+    if (side_plus1) {
+        const float* vals = sm.side[side_plus1 - 1];
+        warp_chain([&](int i) { return vals[i]; }, cnt, s, INFINITY);
+        return s;
+    }
+    float* scratch = reinterpret_cast<float*>(sm.kbuf);
+    const float e = (lane < cnt) ? exact_e(c, sm, __ldg(c.src + base + lane)) : 0.0f;
+    scratch[lane] = e;
+    __syncwarp();
+    warp_chain([&](int i) { return scratch[i]; }, cnt, s, INFINITY);
+    __syncwarp();
+    return s;
+}
+
+// Exact serial softmax denominator from the chunk tables (warp 0).
+__device__ float resolve_S(StreamSmem& sm, const Ctx& c) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.0f;
+    const int nseg = (c.nch + 31) / 32;
+    for (int seg = 0; seg < nseg; ++seg) {
+        const float4 wf = sm.wfn[seg];
+        const uint32_t wz = __float_as_uint(wf.z);
+        if (wz & kFClean) {
+            float s2 = s;
+            if (xm::chain_apply(s2, __float_as_uint(wf.w), xm::ChainFn{wf.x, wf.y, wz & 3u})) {
+                s = s2;
+                continue;
+            }
+        }
+        // chunk-level walk, picking per chunk the function of the current binade
+        const int cnt = min(32, c.nch - seg * 32);
+        const float4 ent = (lane < cnt) ? sm.fn[seg * 32 + lane] : make_float4(0, 0, 0, 0);
+        const uint32_t ez = __float_as_uint(ent.z);
+        float4 aent = make_float4(0, 0, 0, 0);
+        if (lane < cnt && (ez & kFAlt)) aent = sm.alt[(ez >> 8) & 0xFFu];
+        const uint32_t az = __float_as_uint(aent.z);
+        int cpos = 0;
+        while (cpos < cnt) {
+            if (regular_sum(s)) {
+                const uint32_t eb = xm::binade_of(s);
+                const bool use_p = (ez & kFClean) && __float_as_uint(ent.w) == eb;
+                const bool use_a = !use_p && (ez & kFAlt) && (az & kFClean) && __float_as_uint(aent.w) == eb;
+                const bool has = (lane >= cpos) && (lane < cnt) && (use_p || use_a);
+                xm::ChainFn f = xm::chain_identity();
+                if (has) f = use_p ? xm::ChainFn{ent.x, ent.y, ez & 3u} : xm::ChainFn{aent.x, aent.y, az & 3u};
+                const unsigned hm = __ballot_sync(kFullMask, has || lane < cpos);
+                const int fi = (~hm) ? (__ffs(~hm) - 1) : 32;
+                f = warp_incl_compose(f);
+                const float hi = __uint_as_float((eb + 1u) << 23);
+                const float L = (__float_as_uint(s) & 1u) ? f.L1 : f.L0;
+                const bool inb = (lane < cpos) || ((lane < fi) && (L <= __fsub_rn(hi, s)));
+                const unsigned inm = __ballot_sync(kFullMask, inb);
+                const int m = (~inm) ? (__ffs(~inm) - 1) : 32;  // chunks [cpos, m) resolve exactly
+                if (m > cpos) {
+                    s = __shfl_sync(kFullMask, __fadd_rn(s, L), m - 1);
+                    cpos = m;
+                }
+                if (cpos < cnt) {
+                    const uint32_t sp = __shfl_sync(kFullMask, ez >> 16, cpos);
+                    s = replay_chunk(sm, c, seg * 32 + cpos, sp, s);
+                    ++cpos;
+                }
+            } else {
+                const uint32_t sp = __shfl_sync(kFullMask, ez >> 16, cpos);
+                s = replay_chunk(sm, c, seg * 32 + cpos, sp, s);
+                ++cpos;
+            }
+        }
+    }
+    return s;
+}
+
+__device__ void defer_row_s(const RowLaunch& p, int row) {
+    const int k = atomicAdd(p.defer_count, 1);
+    p.defer_rows[k] = row;
+}
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// Loads chunk t (32 floats) with eight independent 16-byte loads.
+__device__ __forceinline__ void load_chunk(const Ctx& c, int t, float (&a)[kSC]) {
+    const int base = t * kSC;
+    const int cnt = min(kSC, c.V - base);  // multiple of 4 when > 0
+#pragma unroll
+    for (int g = 0; g < kSC / 4; ++g) {
+        float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (4 * g < cnt) q = ldg4(c.src + base + 4 * g);
+        a[4 * g] = q.x;
+        a[4 * g + 1] = q.y;
+        a[4 * g + 2] = q.z;
+        a[4 * g + 3] = q.w;
+    }
+}
+
+__global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    StreamSmem& sm = *reinterpret_cast<StreamSmem*>(smem_raw);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid < xm::kExpTableSize) sm.exptab[tid] = xm::exp_table_entry(tid);
+    __syncthreads();
+    const int V = p.vocab;
+    const int nch = (V + kSC - 1) / kSC;
+    // per-CTA L2-resident scratch: the candidate list, then (for nuclei above
+    // the on-chip capacity) the sorted nucleus
+    unsigned long long* super = p.workspace + (long long)blockIdx.x * p.ws_stride;
+
+    for (int row = blockIdx.x; row < p.batch; row += gridDim.x) {
+        Ctx c;
+        c.src = p.logits + (long long)row * p.ld;
+        c.V = V;
+        c.nch = nch;
+        c.T = p.temperature_rows ? p.temperature_rows[row] : p.temperature;
+        const float topp = p.topp_rows ? p.topp_rows[row] : p.topp;
+        const bool greedy = (c.T == 0.0f);
+        if (!greedy && (topp <= 0.0f || topp >= 1.0f)) {  // sample_mult rows: general kernel
+            if (tid == 0) defer_row_s(p, row);
+            continue;
+        }
+
+        if (greedy) {
+            // first index of the strict max, NaN at index 0 wins (llama2.c:981-992)
+            float bv = -INFINITY;
+            int bi = 0x7FFFFFFF;
+            for (int sidx = 0; sidx < kStrips; ++sidx) {
+                const int t = sidx * kST + tid;
+                if (t >= nch) break;
+                float a[kSC];
+                load_chunk(c, t, a);
+                const int cnt = min(kSC, V - t * kSC);
+#pragma unroll
+                for (int j = 0; j < kSC; ++j)
+                    if (j < cnt && (a[j] > bv || (a[j] == bv && t * kSC + j < bi))) {
+                        bv = a[j];
+                        bi = t * kSC + j;
+                    }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const float ov = __shfl_xor_sync(kFullMask, bv, o);
+                const int oi = __shfl_xor_sync(kFullMask, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (lane == 0) {
+                sm.red_a[warp] = bv;
+                sm.red_i[warp] = bi;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                for (int w = 1; w < kSW; ++w)
+                    if (sm.red_a[w] > bv || (sm.red_a[w] == bv && sm.red_i[w] < bi)) {
+                        bv = sm.red_a[w];
+                        bi = sm.red_i[w];
+                    }
+                p.out_ids[row] = (isnan(__ldg(c.src)) || bi == 0x7FFFFFFF) ? 0 : bi;
+                if (p.row_flags) p.row_flags[row] = 0;
+            }
+            __syncthreads();
+            continue;
+        }
+
+        // ---- pass 1: max/min of l; per-chunk approximate sum of exp(x - max)
+        c.rT = __frcp_rn(c.T);
+        c.unit = (c.T == 1.0f);
+        const float k2 = c.rT * 1.4426950408889634f;  // log2(e)/T, approximate scale
+        float mxl = -INFINITY, mnl = INFINITY, M2loc = -3.4e38f;
+        float cm2[kStrips], cs2[kStrips];
+#pragma unroll
+        for (int sidx = 0; sidx < kStrips; ++sidx) {
+            const int t = sidx * kST + tid;
+            float m2 = -3.4e38f, s2 = 0.0f;
+            const int cnt = (t < nch) ? min(kSC, V - t * kSC) : 0;
+            const float* cp = c.src + t * kSC;
+#pragma unroll 2
+            for (int g = 0; g < cnt; g += 4) {
+                const float4 q = ldg4(cp + g);
+                const float a[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    mxl = fmaxf(mxl, a[w]);
+                    mnl = fminf(mnl, a[w]);
+                    const float xs = a[w] * k2;
+                    if (xs > m2) {
+                        s2 = s2 * ex2_approx(m2 - xs);
+                        m2 = xs;
+                    }
+                    s2 += ex2_approx(xs - m2);
+                }
+            }
+            cm2[sidx] = m2;
+            cs2[sidx] = s2;
+            M2loc = fmaxf(M2loc, m2);
+        }
+        float wmx = mxl, wmn = mnl, wm2 = M2loc;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            wmx = fmaxf(wmx, __shfl_xor_sync(kFullMask, wmx, o));
+            wmn = fminf(wmn, __shfl_xor_sync(kFullMask, wmn, o));
+            wm2 = fmaxf(wm2, __shfl_xor_sync(kFullMask, wm2, o));
+        }
+        if (lane == 0) {
+            sm.red_a[warp] = wmx;
+            sm.red_b[warp] = wmn;
+            sm.red_c[warp] = wm2;
+        }
+        if (tid == 0) {
+            sm.n_super = 0;
+            sm.n_alt = 0;
+            sm.n_side = 0;
+            sm.flag = 0;
+            sm.dbin = -1;
+        }
+        for (int b = tid; b < kBins; b += kST) sm.hist[b] = 0;
+        __syncthreads();
+        float MX = -INFINITY, MN = INFINITY, M2 = -3.4e38f;
+#pragma unroll
+        for (int w = 0; w < kSW; ++w) {
+            MX = fmaxf(MX, sm.red_a[w]);
+            MN = fminf(MN, sm.red_b[w]);
+            M2 = fmaxf(M2, sm.red_c[w]);
+        }
+        __syncthreads();  // red_* are reused by the scans below
+        c.max_x = c.unit ? MX : (c.T > 0.0f ? __fdiv_rn(MX, c.T) : __fdiv_rn(MN, c.T));
+        // approximate chunk sums in units of exp(x - max); exclusive prefix in
+        // chunk order (strip-major)
+        float sig[kStrips], gss[kStrips];
+        float strip_off = 0.0f;
+#pragma unroll
+        for (int sidx = 0; sidx < kStrips; ++sidx) {
+            sig[sidx] = cs2[sidx] * ex2_approx(cm2[sidx] - M2);
+            const ScanF sc = block_scan_f(sig[sidx], sm);
+            gss[sidx] = strip_off + sc.excl;
+            strip_off += sc.total;
+        }
+        const float s_approx = strip_off;
+
+        // ---- pass 2: exact e where it matters, chunk functions, candidates
+        const float cutoff = __fdiv_rn(__fsub_rn(1.0f, topp), (float)(V - 1));  // llama2.c:1024
+        const float e_min = cutoff * s_approx * 0.9921875f;
+        const float d_cand = (e_min > 0.0f) ? __logf(e_min) - 1e-3f : -INFINITY;
+        bool nan_any = false;
+#pragma unroll 1
+        for (int sidx = 0; sidx < kStrips; ++sidx) {
+            const int t = sidx * kST + tid;
+            const bool valid = t < nch;
+            const int cnt = valid ? min(kSC, V - t * kSC) : 0;
+            uint32_t alt = 0u;
+            const uint32_t eb = valid ? xm::chain_guess_primary(gss[sidx], sig[sidx], alt) : 0u;
+            // e is absorbed when below half an ulp of a running sum in binade
+            // tb (exp(d) < 2^(tb-151)); never for a possible candidate
+            const uint32_t tb = (eb == 0u) ? 0u : ((alt != 0u && alt < eb) ? alt : eb);
+            const float d_abs = (tb == 0u) ? -INFINITY : ((float)((int)tb - 151) * 0.69314718f - 1e-4f);
+            const float d_thr = fminf(d_abs, d_cand);
+            // chunks whose binade is unknown or near a boundary keep their
+            // values for a possible serial replay (absorbed ones are exact zeros
+            // in every binade at or above tb)
+            float* keep = nullptr;
+            int keep_idx = -1;
+            if (valid && (eb == 0u || alt != 0u)) {
+                keep_idx = atomicAdd(&sm.n_side, 1);
+                if (keep_idx < kSideCap) keep = sm.side[keep_idx];
+                else keep_idx = -1;
+            }
+            const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
+            const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
+            float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
+            const float* cp = c.src + t * kSC;
+#pragma unroll 1
+            for (int g = 0; g < kSC / 4; ++g) {
+                float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (4 * g < cnt) q = ldg4(cp + 4 * g);
+                float a[4] = {q.x, q.y, q.z, q.w};
+                unsigned cm = 0u;
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    float e = 0.0f;
+                    if (4 * g + w < cnt) {
+                        const float x = c.unit ? a[w] : xm_div_const(a[w], c.T, c.rT);
+                        const float d = __fsub_rn(x, c.max_x);
+                        if (!(d < d_thr)) e = xm::exp_f32(d, sm.exptab);
+                        nan_any |= isnan(e);
+                        if (e >= e_min && !isnan(e)) cm |= 1u << w;
+                    }
+                    a[w] = e;
+                    v0 = __fadd_rn(v0, e);
+                    v1 = __fadd_rn(v1, e);
+                    w0 = __fadd_rn(w0, e);
+                    w1 = __fadd_rn(w1, e);
+                }
+                if (keep) reinterpret_cast<float4*>(keep)[g] = make_float4(a[0], a[1], a[2], a[3]);
+                // top-p candidates of this granule, one atomic per warp
+                if (__any_sync(kFullMask, cm != 0u)) {
+                    const int my = __popc(cm);
+                    int incl = my;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int y = __shfl_up_sync(kFullMask, incl, o);
+                        if (lane >= o) incl += y;
+                    }
+                    int b0 = 0;
+                    if (lane == 31) b0 = atomicAdd(&sm.n_super, incl);
+                    b0 = __shfl_sync(kFullMask, b0, 31) + incl - my;
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        if (cm & (1u << w)) {
+                            super[b0++] = cand_key(a[w], t * kSC + 4 * g + w);
+                            atomicAdd(&sm.hist[bin_of(a[w])], 1);
+                        }
+                    }
+                }
+            }
+            // chunk functions (primary and alternative binade)
+            const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
+            const bool aclean = valid && alt != 0u && (__float_as_uint(w0) >> 23) == alt && (__float_as_uint(w1) >> 23) == alt;
+            const xm::ChainFn f{__fsub_rn(v0, lo), __fsub_rn(v1, lo1),
+                                (__float_as_uint(v0) & 1u) | ((__float_as_uint(v1) & 1u) << 1)};
+            uint32_t z = (clean ? (f.pbits | kFClean) : 0u) | (valid ? kFValid : 0u);
+            if (aclean) {
+                const int ai = atomicAdd(&sm.n_alt, 1);
+                if (ai < kAltCap) {
+                    sm.alt[ai] = make_float4(__fsub_rn(w0, alo), __fsub_rn(w1, alo1),
+                                             __uint_as_float((__float_as_uint(w0) & 1u) |
+                                                             ((__float_as_uint(w1) & 1u) << 1) | kFClean),
+                                             __uint_as_float(alt));
+                    z |= kFAlt | ((uint32_t)ai << 8);
+                }
+            }
+            if (keep_idx >= 0) z |= (uint32_t)(keep_idx + 1) << 16;
+            if (valid) sm.fn[t] = make_float4(f.L0, f.L1, __uint_as_float(z), __uint_as_float(eb));
+            // segment (= warp within the strip) function when all chunks are
+            // clean in one binade
+            const uint32_t eb0 = __shfl_sync(kFullMask, eb, 0);
+            const bool uni = __all_sync(kFullMask, !valid || (clean && eb == eb0 && !(z & kFAlt)));
+            const xm::ChainFn F = warp_incl_compose((valid && clean) ? f : xm::chain_identity());
+            if (lane == 31)
+                sm.wfn[sidx * kSW + warp] =
+                    make_float4(F.L0, F.L1, __uint_as_float(F.pbits | (uni ? kFClean : 0u)), __uint_as_float(eb0));
+        }
+        const bool row_nan = __syncthreads_or(nan_any) != 0;
+
+        // ---- coin (drawn before the walk, llama2.c:1094); state committed at the end
+        unsigned long long st = 0;
+        float coin = 0.0f;
+        if (p.coins) {
+            coin = p.coins[row];
+        } else {
+            st = p.rng_state[row];
+            coin = draw_coin(st);
+        }
+        int flags = 0, id = 0;
+        bool defer = false;
+        if (row_nan) {
+            flags = kFlagNan | kFlagNoCand;
+        } else {
+            // ---- exact S
+            if (warp == 0) {
+                const float S = resolve_S(sm, c);
+                if (lane == 0) sm.fval = S;
+            }
+            __syncthreads();
+            const float S = sm.fval;
+            // ---- nucleus selection: guaranteed mass of bins 0..D
+            int h[kBinsPerThread];
+            int hc = 0, nsort = 0;
+            float hm = 0.0f;
+#pragma unroll
+            for (int q = 0; q < kBinsPerThread; ++q) {
+                const int b = tid * kBinsPerThread + q;
+                h[q] = sm.hist[b];
+                hc += h[q];
+                hm += (float)h[q] * bin_lo(b);
+            }
+            const ScanF ms = block_scan_f(hm, sm);
+            int ctot;
+            const int cex = block_scan_i(hc, sm, ctot) - hc;
+            const float target = (topp + 4096.0f * 0x1p-24f + 1e-5f) * S * 1.0000005f;
+            if (ms.incl >= target && ms.excl < target) {
+                float m = ms.excl;
+                int cc = cex, d = tid * kBinsPerThread + kBinsPerThread - 1;
+#pragma unroll
+                for (int q = 0; q < kBinsPerThread; ++q) {
+                    cc += h[q];
+                    m += (float)h[q] * bin_lo(tid * kBinsPerThread + q);
+                    if (m >= target) {
+                        d = tid * kBinsPerThread + q;
+                        break;
+                    }
+                }
+                sm.dbin = d;
+                sm.ksel = cc;
+            }
+            __syncthreads();
+            int D = sm.dbin, K = sm.ksel;
+            const bool all_cand = D < 0;
+            if (all_cand) {
+                D = kBins - 1;
+                K = ctot;
+            }
+            const int nsup = sm.n_super;
+            // the nucleus lives on chip, or after the candidate list in L2
+            unsigned long long* kb = (K <= kKCap) ? sm.kbuf : super + ((nsup + 1) & ~1);
+            if (K > 4096) {  // beyond the drift bound the selection margin covers
+                defer = true;
+            } else {
+                // bin offsets (hist becomes the scatter cursor) and the list of
+                // bins that need sorting (kept in the side area)
+                int run = cex;
+#pragma unroll
+                for (int q = 0; q < kBinsPerThread; ++q) {
+                    const int b = tid * kBinsPerThread + q;
+                    if (b <= D) {
+                        sm.bstart[b] = (short)run;
+                        sm.hist[b] = run;
+                        run += h[q];
+                        nsort += (h[q] >= 2) ? 1 : 0;
+                    }
+                }
+                int nlist;
+                int wpos = block_scan_i(nsort, sm, nlist) - nsort;
+                int* list = reinterpret_cast<int*>(&sm.side[0][0]);
+#pragma unroll
+                for (int q = 0; q < kBinsPerThread; ++q) {
+                    const int b = tid * kBinsPerThread + q;
+                    if (b <= D && h[q] >= 2) list[wpos++] = b;
+                }
+                for (int i = tid; i < nsup; i += kST) {
+                    const unsigned long long k = super[i];
+                    const int b = bin_of(key_prob(k));
+                    if (b <= D) {
+                        const int pos = atomicAdd(&sm.hist[b], 1);
+                        if (pos < K) kb[pos] = k;
+                    }
+                }
+                if (tid == 0) sm.flag = 0;
+                __syncthreads();
+                // sort each bin by (e desc, index asc)
+                for (int q = warp; q < nlist; q += kSW) {
+                    const int b = list[q];
+                    const int s0 = sm.bstart[b];
+                    const int n = sm.hist[b] - s0;
+                    if (s0 < 0 || s0 + n > K) {
+                        if (lane == 0) sm.flag = 1;
+                        continue;
+                    }
+                    unsigned long long* seg = kb + s0;
+                    if (n <= 32) warp_sort_desc<1>(seg, n, lane);
+                    else if (n <= 64) warp_sort_desc<2>(seg, n, lane);
+                    else if (n <= 128) warp_sort_desc<4>(seg, n, lane);
+                    else if (n <= 256) warp_sort_desc<8>(seg, n, lane);
+                    else if (lane == 0) sm.flag = 1;
+                }
+                __syncthreads();
+                if (sm.flag) {
+                    defer = true;
+                } else {
+                    // p = fl(e/S) in place of e; flag equal-p runs out of index order
+                    bool bad = false;
+                    for (int i = tid; i < K; i += kST) {
+                        const unsigned long long k = kb[i];
+                        const float pv = __fdiv_rn(key_prob(k), S);
+                        kb[i] = ((unsigned long long)__float_as_uint(pv) << 32) | (k & 0xFFFFFFFFull);
+                    }
+                    __syncthreads();
+                    for (int i = tid; i + 1 < K; i += kST) {
+                        const unsigned long long a = kb[i], b = kb[i + 1];
+                        bad |= ((a >> 32) == (b >> 32)) && (key_index(a) > key_index(b));
+                    }
+                    if (__syncthreads_or(bad) && tid == 0) {
+                        for (bool swapped = true; swapped;) {
+                            swapped = false;
+                            for (int i = 0; i + 1 < K; ++i) {
+                                const unsigned long long a = kb[i], b = kb[i + 1];
+                                if ((a >> 32) == (b >> 32) && key_index(a) > key_index(b)) {
+                                    kb[i] = b;
+                                    kb[i + 1] = a;
+                                    swapped = true;
+                                }
+                            }
+                        }
+                    }
+                    __syncthreads();
+                    // candidates proper (p >= cutoff) form a prefix
+                    int n0loc = 0;
+                    for (int i = tid; i < K; i += kST) n0loc += (key_prob(kb[i]) >= cutoff) ? 1 : 0;
+                    int n0;
+                    block_scan_i(n0loc, sm, n0);
+                    if (warp == 0) {
+                        int res = -1;
+                        if (n0 == 0) {
+                            res = all_cand ? -2 : -1;
+                        } else {
+                            auto get = [&](int i) { return key_prob(kb[i]); };
+                            float cum = 0.0f;
+                            int last = warp_chain(get, n0, cum, topp);  // llama2.c:1036-1043
+                            if (last >= n0) last = all_cand ? n0 - 1 : -1;  // llama2.c:1037
+                            if (last >= 0) {
+                                const float r = __fmul_rn(coin, cum);  // llama2.c:1046
+                                float s3 = 0.0f;
+                                int k = warp_chain(get, last + 1, s3, r);
+                                if (k > last) k = last;  // llama2.c:1055
+                                res = key_index(kb[k]);
+                            }
+                        }
+                        if (lane == 0) sm.result = res;
+                    }
+                    __syncthreads();
+                    const int res = sm.result;
+                    if (res == -1) {
+                        defer = true;
+                    } else if (res == -2) {
+                        flags |= kFlagNoCand;
+                        id = 0;
+                    } else {
+                        id = res;
+                    }
+                }
+            }
+        }
+        if (tid == 0) {
+            if (defer) {
+                defer_row_s(p, row);
+            } else {
+                p.out_ids[row] = id;
+                if (p.row_flags) p.row_flags[row] = flags;
+                if (!p.coins) p.rng_state[row] = st;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+size_t stream_smem_bytes() { return sizeof(StreamSmem); }
+int stream_ctas_per_sm() { return 4; }
+
+int launch_row_stream(const RowLaunch& p, int num_ctas, cudaStream_t stream) {
+    static std::atomic<unsigned long long> attr_done{0};
+    int dev = 0;
+    cudaError_t e0 = cudaGetDevice(&dev);
+    if (e0 != cudaSuccess) return -(int)e0;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(attr_done.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(row_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(StreamSmem));
+        if (e != cudaSuccess) return -(int)e;
+        attr_done.fetch_or(bit);
+    }
+    row_stream_kernel<<<num_ctas, kST, sizeof(StreamSmem), stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 1 : -(int)e;
+}
+
+}  // namespace b2s

@@ -122,7 +122,27 @@ int ensure_row(DeviceCtx* c, int V) {
 
 int row_ctas(const DeviceCtx* c, int batch) { return batch < c->num_sms ? batch : c->num_sms; }
 
-size_t workspace_for(int ctas, int V) { return (size_t)ctas * next_pow2((size_t)V) * sizeof(unsigned long long); }
+// Workspace layout: [deferred-row count (16 B)][deferred rows: batch int32,
+// padded to 16 B][general kernel: ctas x pow2(V) u64 sort scratch]
+// [streaming kernel: stream_ctas x V u64 candidate lists].
+size_t defer_bytes(int batch) { return 16 + (((size_t)batch * sizeof(int) + 15) & ~(size_t)15); }
+size_t general_bytes(int ctas, int V) { return (size_t)ctas * next_pow2((size_t)V) * sizeof(unsigned long long); }
+// per streaming CTA: the candidate list (<= V keys) and a nucleus spill area
+size_t stream_stride(int V) { return (size_t)((V + 1) & ~1) + 4096; }
+size_t stream_bytes(int sctas, int V) { return (size_t)sctas * stream_stride(V) * sizeof(unsigned long long); }
+int stream_ctas(const DeviceCtx* c, int batch) {
+    const int n = c->num_sms * b2s::stream_ctas_per_sm();
+    return batch < n ? batch : n;
+}
+size_t workspace_for(const DeviceCtx* c, int V, int batch) {
+    const int ctas = batch < c->num_sms ? batch : c->num_sms;
+    return defer_bytes(batch) + general_bytes(ctas, V) + stream_bytes(stream_ctas(c, batch), V);
+}
+
+// Rows the streaming kernel can stage with 16-byte vector loads.
+bool stream_layout_ok(const float* logits, int V, long long ld) {
+    return (V % 4) == 0 && V <= SAMPLER_MAX_VOCAB && (ld % 4) == 0 && ((uintptr_t)logits & 15u) == 0;
+}
 
 // Core dispatcher shared by every entry point.  All pointers are device
 // pointers.  force_mode: 0 = sample() dispatch by topp, 1 = sample_mult,
@@ -156,7 +176,7 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
     }
 
     const int ctas = row_ctas(c, batch);
-    const size_t need = workspace_for(ctas, V);
+    const size_t need = workspace_for(c, V, batch);
     unsigned long long* ws = nullptr;
     if (workspace) {
         if (workspace_bytes < need)
@@ -169,6 +189,12 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
         if (rc) return rc;
         ws = c->workspace;
     }
+    char* wsb = reinterpret_cast<char*>(ws);
+    int* defer_count = reinterpret_cast<int*>(wsb);
+    int* defer_rows = reinterpret_cast<int*>(wsb + 16);
+    unsigned long long* general_ws = reinterpret_cast<unsigned long long*>(wsb + defer_bytes(batch));
+    unsigned long long* stream_ws =
+        reinterpret_cast<unsigned long long*>(wsb + defer_bytes(batch) + general_bytes(ctas, V));
     b2s::RowLaunch p{};
     p.logits = logits;
     p.ld = ld;
@@ -183,14 +209,33 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
     p.out_ids = out_ids;
     p.probs_out = probs_out;
     p.row_flags = row_flags;
-    p.workspace = ws;
+    p.workspace = general_ws;
     p.ws_stride = (long long)next_pow2((size_t)V);
     p.probs_in = probs_in ? 1 : 0;
     p.force_mode = force_mode;
     p.error_word = c->error_word;
+    p.defer_count = defer_count;
+    p.defer_rows = defer_rows;
+    // Fast path: the streaming kernel takes greedy and top-p rows and defers
+    // the rest to the general kernel, which then walks the deferred list.
+    // Probabilities in/out and forced modes use the general kernel for every
+    // row.
+    const bool streamed = !probs_in && !probs_out && force_mode == 0 && stream_layout_ok(logits, V, ld);
+    int launches = 0;
+    if (streamed) {
+        B2S_CUDA(cudaMemsetAsync(defer_count, 0, sizeof(int), stream));
+        b2s::RowLaunch q = p;
+        q.workspace = stream_ws;
+        q.ws_stride = (long long)stream_stride(V);
+        const int n = b2s::launch_row_stream(q, stream_ctas(c, batch), stream);
+        if (n < 0) return fail(SAMPLER_E_CUDA, "stream launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+        launches += n + 1;
+        p.row_list = defer_rows;
+        p.row_count = defer_count;
+    }
     const int n = b2s::launch_row_sampler(p, ctas, stream);
     if (n < 0) return fail(SAMPLER_E_CUDA, "row sampler launch: %s", cudaGetErrorString((cudaError_t)(-n)));
-    g_last_launches = n;
+    g_last_launches = launches + n;
     return SAMPLER_OK;
 }
 
@@ -345,10 +390,8 @@ int sample(Sampler* sampler, float* logits) {
 // ===========================================================================
 size_t sampler_workspace_bytes(int batch, int vocab_size) {
     DeviceCtx* c = nullptr;
-    int sms = 148;
-    if (get_ctx(&c) == SAMPLER_OK) sms = c->num_sms;
-    const int ctas = batch < sms ? (batch < 1 ? 1 : batch) : sms;
-    return workspace_for(ctas, vocab_size < 1 ? 1 : vocab_size);
+    if (get_ctx(&c) != SAMPLER_OK || !c) return 0;
+    return workspace_for(c, vocab_size < 1 ? 1 : vocab_size, batch < 1 ? 1 : batch);
 }
 
 int sampler_batched(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
@@ -373,7 +416,9 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
     if (!all_greedy && !rng_state) return fail(SAMPLER_E_INVALID, "rng_state is NULL");
     // Each of the two pipeline streams gets its own half of the workspace so
     // two chunks in flight never share slow-path scratch.
-    const size_t ws_half = workspace_for(row_ctas(c, batch), V);
+    int chunk = (batch + 7) / 8;  // about eight chunks, each at least one CTA per SM
+    if (chunk < c->num_sms) chunk = batch < c->num_sms ? batch : c->num_sms;
+    const size_t ws_half = (workspace_for(c, V, chunk) + 255) & ~(size_t)255;
     {
         std::lock_guard<std::mutex> lk(g_mu);
         rc = ensure_workspace(c, 2 * ws_half);
@@ -402,8 +447,6 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
     }
     // Chunks of rows alternate between two streams: the copy of chunk k+1
     // overlaps the sampling of chunk k.
-    int chunk = (batch + 7) / 8;  // about eight chunks, each at least one CTA per SM
-    if (chunk < c->num_sms) chunk = batch < c->num_sms ? batch : c->num_sms;
     int launches = 0;
     for (int r0 = 0, k = 0; r0 < batch; r0 += chunk, ++k) {
         const int rows = (batch - r0) < chunk ? (batch - r0) : chunk;

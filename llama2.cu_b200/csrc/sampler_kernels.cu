@@ -26,6 +26,7 @@
 //      and the r = coin*cum walk over that sorted nucleus only.
 //   Nuclei beyond the on-chip capacity take a global-memory path (sort in the
 //   per-CTA workspace, engine over 8192-element pieces).
+#include "device_common.cuh"
 #include "exact_math.cuh"
 #include "sampler_kernels.cuh"
 
@@ -38,18 +39,10 @@ namespace b2s {
 namespace {
 
 constexpr int kWarps = kRowThreads / 32;
-constexpr int kBins = 2048;
-constexpr int kBinShift = 17;  // 64 bins per binade of p
-constexpr uint32_t kOneTop = 0x3F800000u >> kBinShift;
 constexpr int kSegSortMax = 256;
 constexpr int kMaxBigSegs = 64;
 constexpr int kTmaParts = 4;
 constexpr int kMaxPieces = 8;
-constexpr unsigned kSpinLimit = 1u << 22;  // polls of a bounded mbarrier wait (~0.5 s)
-constexpr uint32_t kFullMask = 0xFFFFFFFFu;
-
-// Row flags (mirrors of the public SAMPLER_ROW_* values)
-constexpr int kFlagNan = 1, kFlagNoCand = 2, kFlagSlow = 4, kFlagSerial = 8, kFlagTimeout = 16;
 
 struct __align__(16) RowSmem {
     float row[kRowCap];                     // staged logits / e / p (swizzled chunks)
@@ -84,67 +77,6 @@ struct __align__(16) RowSmem {
 // ---------------------------------------------------------------------------
 // small helpers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, unsigned bytes,
-                                              unsigned long long* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait: gives up after kSpinLimit polls instead of hanging the SM.
-__device__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity) {
-    for (unsigned i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (i > 32) __nanosleep(64);
-    }
-    return false;
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void fence_mbar_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-// xorshift* draw + 24-bit float, llama2.c:1071-1080.
-__device__ __forceinline__ float draw_coin(unsigned long long& s) {
-    s ^= s >> 12;
-    s ^= s << 25;
-    s ^= s >> 27;
-    const unsigned u = (unsigned)((s * 0x2545F4914F6CDD1Dull) >> 32);
-    return __fdiv_rn((float)(u >> 8), 16777216.0f);
-}
-
 // Physical float4 granule of logical granule g of chunk t, for chunks of
 // CPT floats (G = CPT/4 granules).  The XOR keeps the 8 threads of a
 // quarter-warp on distinct 16-byte bank groups when each reads its own chunk.
@@ -362,79 +294,6 @@ __device__ void chain_find(RowSmem& sm, int nch, float theta) {
 // ---------------------------------------------------------------------------
 // Sorting of 64-bit keys, descending
 // ---------------------------------------------------------------------------
-template <int R>
-__device__ void warp_sort_desc(unsigned long long* seg, int n, int lane) {
-    constexpr int P = 32 * R;
-    unsigned long long k[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-        const int i = r * 32 + lane;
-        k[r] = (i < n) ? seg[i] : 0ull;
-    }
-#pragma unroll
-    for (int size = 2; size <= P; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            unsigned long long nk[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int i = r * 32 + lane;
-                unsigned long long other;
-                if (stride >= 32) {
-                    other = k[r ^ (stride >> 5)];
-                } else {
-                    other = __shfl_xor_sync(kFullMask, k[r], stride);
-                }
-                const bool desc = (i & size) == 0;
-                const bool lower = (i & stride) == 0;
-                const bool take_max = (lower == desc);
-                nk[r] = take_max ? (k[r] > other ? k[r] : other) : (k[r] < other ? k[r] : other);
-            }
-#pragma unroll
-            for (int r = 0; r < R; ++r) k[r] = nk[r];
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-        const int i = r * 32 + lane;
-        if (i < n) seg[i] = k[r];
-    }
-}
-
-// Block-wide bitonic sort (descending) of a power-of-two array `a` of P keys.
-// Works for shared or global memory (the block barrier orders both).
-__device__ void block_bitonic_desc(unsigned long long* a, int P) {
-    for (int size = 2; size <= P; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int q = threadIdx.x; q < (P >> 1); q += blockDim.x) {
-                const int i = 2 * stride * (q / stride) + (q % stride);
-                const int l = i + stride;
-                const bool desc = (i & size) == 0;
-                const unsigned long long x = a[i], y = a[l];
-                if (desc ? (x < y) : (x > y)) {
-                    a[i] = y;
-                    a[l] = x;
-                }
-            }
-            __syncthreads();
-        }
-    }
-}
-
-__device__ __forceinline__ unsigned long long cand_key(float p, int idx) {
-    return ((unsigned long long)__float_as_uint(p) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
-}
-__device__ __forceinline__ float key_prob(unsigned long long k) { return __uint_as_float((uint32_t)(k >> 32)); }
-__device__ __forceinline__ int key_index(unsigned long long k) { return (int)(0xFFFFFFFFu - (uint32_t)k); }
-
-__device__ __forceinline__ int bin_of(float p) {
-    const int b = (int)kOneTop - (int)(__float_as_uint(p) >> kBinShift);
-    return b < 0 ? 0 : (b >= kBins ? kBins - 1 : b);
-}
-__device__ __forceinline__ float bin_lo(int b) {
-    return (b >= kBins - 1) ? 0.0f : __uint_as_float((kOneTop - (uint32_t)b) << kBinShift);
-}
-
 // Writes p values of sorted keys [first, first+count) from `src` into sm.row
 // in the CPT=8 chunk layout (zero padded to whole chunks); returns #chunks.
 __device__ int stage_sorted_probs(RowSmem& sm, const unsigned long long* src, int count) {
@@ -956,7 +815,9 @@ __global__ void __launch_bounds__(kRowThreads, 1) row_sampler_kernel(RowLaunch p
     unsigned long long* ws = p.workspace ? p.workspace + (long long)blockIdx.x * p.ws_stride : nullptr;
 
     unsigned phase = 0;
-    for (int row = blockIdx.x; row < p.batch; row += gridDim.x) {
+    const int nrows = p.row_list ? *p.row_count : p.batch;
+    for (int it = blockIdx.x; it < nrows; it += gridDim.x) {
+        const int row = p.row_list ? p.row_list[it] : it;
         const float* src = p.logits + (long long)row * p.ld;
         int flags = 0;
 

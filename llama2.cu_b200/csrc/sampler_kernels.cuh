@@ -30,6 +30,12 @@ struct RowLaunch {
     int probs_in;                 // rows are probabilities
     int force_mode;               // 0: by topp as sample() does, 1: sample_mult, 2: sample_topp
     int* error_word;              // device word, set on bounded-wait timeout
+    // deferred rows: the streaming kernel appends rows it leaves to the
+    // general kernel; the general kernel then walks row_list[0..*row_count)
+    int* defer_count;
+    int* defer_rows;
+    const int* row_list;
+    const int* row_count;
 };
 
 struct ArgmaxLaunch {
@@ -47,5 +53,11 @@ int launch_argmax(const ArgmaxLaunch& p, cudaStream_t stream);
 int launch_seed_states(unsigned long long* st, int batch, unsigned long long seed,
                        long long offset, cudaStream_t stream);
 size_t row_kernel_smem_bytes();
+size_t stream_smem_bytes();
+int stream_ctas_per_sm();
+// The streaming kernel over all rows (greedy and top-p rows finish there;
+// the rest go to the deferred list).  workspace: ws_stride >= vocab u64
+// entries per CTA.
+int launch_row_stream(const RowLaunch& p, int num_ctas, cudaStream_t stream);
 
 }  // namespace b2s

@@ -64,6 +64,8 @@ def prob_rel_err(p, ref):
 
 
 def check_e2e(orc, got, ref_ids, ref_probs, seeds, topps):
+    if len(ref_ids) == 0:
+        return 0
     mism = np.nonzero(got != ref_ids)[0]
     assert 1.0 - len(mism) / len(ref_ids) >= MIN_MATCH, f"{len(mism)} mismatching ids of {len(ref_ids)}"
     for r in mism:
@@ -155,6 +157,53 @@ def test_topp_workload_end_to_end(pkg, orc, golden):
     check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, w["topp_rows"])
 
 
+def test_topp_workload_pipelined_path(pkg, orc, golden):
+    """Without probability write-back the batch takes the pipelined kernel
+    (rows it defers finish in the general kernel)."""
+    w = pkg.workloads.topp()
+    seeds = pkg.workloads.row_seeds(4096)
+    out = gpu_sample(pkg, w["logits"], w["temperature"], w["topp"], seeds=seeds, topp_rows=w["topp_rows"])
+    ref_ids, ref_st, ref_p = orc.sample_batch(w["logits"], w["temperature"], w["topp"], seeds,
+                                              topp_rows=w["topp_rows"], probs_out=True)
+    assert np.array_equal(out["states"], ref_st)
+    assert (out["flags"] >= 0).all()
+    check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, w["topp_rows"])
+
+
+def test_mixed_modes_in_one_batch(pkg, orc):
+    """Greedy, top-p and multinomial rows together (per-row temperature and
+    topp): the pipelined kernel takes greedy and top-p rows and defers the
+    multinomial ones."""
+    rng = np.random.default_rng(41)
+    B = 300
+    x = rng.normal(0, 2.5, (B, 32000)).astype(np.float32)
+    temps = np.where(np.arange(B) % 5 == 0, 0.0, 0.9).astype(np.float32)
+    topps = np.where(np.arange(B) % 3 == 0, 1.0, 0.9).astype(np.float32)
+    seeds = np.arange(B, dtype=np.uint64) * 7 + 3
+    out = gpu_sample(pkg, x, 0.9, 0.9, seeds=seeds, topp_rows=topps, temp_rows=temps)
+    ids, states = [], []
+    for r in range(B):
+        i, s_ = orc.sample_batch(x[r:r + 1], float(temps[r]), float(topps[r]), seeds[r:r + 1])
+        ids.append(int(i[0]))
+        states.append(int(s_[0]))
+    assert np.array_equal(out["states"], np.array(states, np.uint64))
+    mism = [r for r in range(B) if out["ids"][r] != ids[r]]
+    for r in mism:
+        _, _, rp = orc.sample_batch(x[r:r + 1], float(temps[r]), float(topps[r]), seeds[r:r + 1], probs_out=True)
+        coin, _ = orc.coin(int(seeds[r]))
+        assert temps[r] != 0.0 and orc.boundary_distance(rp[0], float(topps[r]), coin) <= BOUNDARY
+
+
+def test_large_nucleus_deferred_from_pipeline(pkg, orc):
+    x = np.random.default_rng(15).normal(0, 0.05, (8, 32000)).astype(np.float32)
+    seeds = np.arange(8, dtype=np.uint64) + 100
+    out = gpu_sample(pkg, x, 1.0, 0.95, seeds=seeds)
+    assert (out["flags"] & pkg.ROW_SLOW_PATH).all()
+    ref_ids, ref_st, ref_p = orc.sample_batch(x, 1.0, 0.95, seeds, probs_out=True)
+    assert np.array_equal(out["states"], ref_st)
+    check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, np.full(8, 0.95))
+
+
 def test_topp_without_probability_writeback_same_ids(pkg):
     """The fast path (no probs_out) computes p only for candidates; ids must
     not change."""
@@ -223,6 +272,12 @@ EDGE = [
 ]
 
 
+EDGE_CASES_FAST = EDGE + [
+    ("nan_in_topp_row", lambda r: np.tile(np.array([1.0, np.nan] + [0.5] * 30, np.float32), (r, 1)), 1.0, 0.9),
+    ("one_hot", lambda r: np.where(np.arange(32000) == 777, 30.0, 0.0).astype(np.float32)[None, :].repeat(r, 0), 1.0, 0.9),
+]
+
+
 @pytest.mark.parametrize("name,make,temp,topp", EDGE)
 def test_edge_cases(pkg, orc, name, make, temp, topp):
     x = make(24)
@@ -279,3 +334,17 @@ def test_repeatable(pkg):
     a = gpu_sample(pkg, w["logits"], 0.7, 0.9, seeds=seeds, topp_rows=w["topp_rows"])
     b = gpu_sample(pkg, w["logits"], 0.7, 0.9, seeds=seeds, topp_rows=w["topp_rows"])
     assert np.array_equal(a["ids"], b["ids"]) and np.array_equal(a["states"], b["states"])
+
+
+@pytest.mark.parametrize("name,make,temp,topp", EDGE_CASES_FAST)
+def test_edge_cases_pipelined(pkg, orc, name, make, temp, topp):
+    x = make(24)
+    seeds = np.arange(24, dtype=np.uint64) * 11 + 5
+    out = gpu_sample(pkg, x, temp, topp, seeds=seeds)
+    ref_ids, ref_st, ref_p = orc.sample_batch(x, temp, topp, seeds, probs_out=True)
+    assert np.array_equal(out["states"], ref_st)
+    nan_rows = np.isnan(ref_p).any(axis=1)
+    keep = ~nan_rows if (nan_rows.any() and 0 < topp < 1) else np.ones(len(x), bool)
+    if nan_rows.any() and 0 < topp < 1:
+        assert (out["flags"][nan_rows] & pkg.ROW_NO_CANDIDATE).all()
+    check_e2e(orc, out["ids"][keep], ref_ids[keep], ref_p[keep], seeds[keep], np.full(keep.sum(), topp))
