@@ -152,6 +152,30 @@ int sampler_last_launch_count(void);
 /* Human-readable text of the last error on this thread. */
 const char* sampler_last_error(void);
 
+/* Largest vocabulary sampler_batched_noalloc accepts. */
+#define SAMPLER_NOALLOC_MAX_VOCAB 32768
+
+/* The batched sampler for callers that cannot allocate device memory (an
+ * inference server whose GPU memory belongs to its own arena or caching
+ * allocator, or a decode loop that must not let cudaMalloc/cudaFree
+ * synchronize the device).  No counterpart in the reference.  Same
+ * arguments and per-row semantics as sampler_batched, without the workspace:
+ * it allocates nothing (no cudaMalloc/cudaFree, no allocating library call)
+ * and uses a fixed 8 MiB + 256 B array compiled into the library, present on
+ * every GPU that loads it until the process exits.
+ *  - vocab_size above SAMPLER_NOALLOC_MAX_VOCAB: returns SAMPLER_E_UNSUPPORTED.
+ *  - The first call on each device looks up that device's copy of the array
+ *    (cudaGetSymbolAddress) with the device current; make that first call
+ *    before any stream capture.
+ *  - Every call shares the array (it keeps the last call's contents), so
+ *    calls that overlap on the GPU -- different streams, or threads using the
+ *    same device -- race; serialize them.
+ *  - Returns status codes only; sampler_last_error() is not updated. */
+int sampler_batched_noalloc(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
+                            const float* temperature_rows, const float* topp_rows, const float* coins,
+                            unsigned long long* rng_state, int* out_ids, float* probs_out, int* row_flags,
+                            void* stream);
+
 /* ------------------------------------------------------------------------
  * Multi-GPU helpers (no counterpart in the reference, which is single-GPU:
  * llama2_cublas.cu:6065 calls cudaSetDevice(0)).

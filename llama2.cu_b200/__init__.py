@@ -22,7 +22,7 @@ EXPORTED_SYMBOLS = [
     "sample_topp", "sample", "sampler_workspace_bytes", "sampler_batched", "sampler_batched_host",
     "sampler_seed_states", "sampler_last_launch_count", "sampler_last_error", "sampler_shard_rows",
     "sampler_nccl_get_unique_id", "sampler_nccl_comm_init", "sampler_nccl_allgather_ids",
-    "sampler_nccl_comm_destroy",
+    "sampler_nccl_comm_destroy", "sampler_batched_noalloc",
 ]
 
 
