@@ -8,26 +8,31 @@
 // with eight independent 16-byte loads.
 //
 //   Pass 1 (HBM read): max/min of the logits and, per chunk, an approximate
-//     online sum of exp(x - max) (ex2.approx) -- only used to guess which
-//     binade the serial running sum sits in at every chunk.
-//   Pass 2 (the same bytes, now in L2): x = l/T (Markstein division) and
-//     d = x - max.  An element whose e = exp(d) is provably below half an ulp
-//     of the (guessed) running sum is absorbed by the serial fp32 sum --
-//     llama2.c's loop adds it and nothing changes -- so its exact e is never
-//     needed: e = 0 stands in for it.  Everything else gets the exact
-//     table-driven exp.  The binade-chain function of the chunk is built on
-//     the fly (exact_math.cuh), plus an alternative for the neighbouring
-//     binade when the guess lies near a boundary.  Top-p candidates
-//     (e >= cutoff*S, with margin) go to an L2-resident per-CTA list and a
-//     histogram over the top bits of e.
-//   Resolution (one warp): chunk functions -> the exact serial softmax
-//     denominator S; chunks that straddle a binade are replayed by a
-//     warp-cooperative exact chain.
-//   Nucleus: the smallest prefix of histogram bins whose guaranteed mass
-//     exceeds topp plus the fp32 drift bound is scattered on chip in bin
-//     order, each bin sorted by (e desc, index asc), p = fl(e/S), equal-p runs
-//     put in index order (glibc qsort's order), and the warp-cooperative
-//     chain walks the serial cumulative sum to topp and then to r = coin*cum.
+//     online sum of exp(x - max) (ex2.approx) -- used to guess which binade
+//     the serial running sum sits in at every chunk, and as S_approx.
+//   Pass 2 (the same bytes, now in L2; three 16-byte loads in flight per
+//     thread): x = l/T (Markstein division) and d = x - max.  An element
+//     whose e = exp(d) is provably below half an ulp of the (guessed) running
+//     sum is absorbed by the serial fp32 sum -- llama2.c's loop adds it and
+//     nothing changes -- so its exact e is never needed: e = 0 stands in for
+//     it.  Everything else gets the exact table-driven exp.  The binade-chain
+//     function of the chunk is built on the fly (exact_math.cuh), plus an
+//     alternative for the neighbouring binade when the guess lies near a
+//     boundary.  Possible top-p candidates (e >= cutoff*S_approx, with margin)
+//     are counted in a histogram over the top bits of e.
+//   Nucleus bins: the smallest prefix of histogram bins whose guaranteed mass
+//     exceeds topp plus the fp32 drift bound, against S_approx scaled up by a
+//     2^-7 margin.
+//   Then, concurrently: warp 0 turns the chunk functions into the exact
+//     serial softmax denominator S (chunks that straddle a binade are
+//     replayed by a warp-cooperative exact chain), while warps 1-7 re-read
+//     the row from L2, scatter the elements of the nucleus bins in bin order
+//     and sort each bin by (e desc, index asc).
+//   Walk: p = fl(e/S), equal-p runs put in index order (glibc qsort's
+//     order), and the warp-cooperative chain walks the serial cumulative sum
+//     to topp and then to r = coin*cum.  A walk that does not cross topp
+//     inside the selected bins (S_approx was off by more than the margin)
+//     defers the row.
 // Rows this kernel does not finish (sample_mult rows, nuclei above the
 // on-chip capacity, failed guesses without stored values) are appended to
 // the deferred-row list that the general row kernel processes next.
@@ -62,6 +67,7 @@ struct StreamSmem {
     int hist[kBins];
     short bstart[kBins];
     float side[kSideCap][kSC];
+    float replay[kSC];
     float4 fn[kChunks];
     float4 alt[kAltCap];
     float4 wfn[kSegs];
@@ -71,7 +77,6 @@ struct StreamSmem {
     float red_c[kSW];
     float red_s[kStrips][kSW];
     int red_i[kSW];
-    int n_super;
     int n_alt;
     int n_side;
     int flag;
@@ -80,6 +85,9 @@ struct StreamSmem {
     int result;
     float fval;
 };
+
+// Four CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per CTA.
+static_assert(4 * (sizeof(StreamSmem) + 1024) <= 228 * 1024, "StreamSmem too large for 4 CTAs per SM");
 
 struct Ctx {
     const float* src;  // row
@@ -248,7 +256,7 @@ __device__ __forceinline__ float exact_e(const Ctx& c, const StreamSmem& sm, flo
 }
 
 // Replays chunk t exactly starting from s (warp 0): kept values, or values
-// recomputed from the row (no absorption) into the warp's scratch.
+// recomputed from the row (no absorption) into the replay scratch.
 __device__ float replay_chunk(StreamSmem& sm, const Ctx& c, int t, uint32_t side_plus1, float s) {
     const int lane = threadIdx.x & 31;
     const int base = t * kSC;
@@ -258,7 +266,7 @@ __device__ float replay_chunk(StreamSmem& sm, const Ctx& c, int t, uint32_t side
         warp_chain([&](int i) { return vals[i]; }, cnt, s, INFINITY);
         return s;
     }
-    float* scratch = reinterpret_cast<float*>(sm.kbuf);
+    float* scratch = sm.replay;  // warp 0's own: the other warps fill kbuf meanwhile
     const float e = (lane < cnt) ? exact_e(c, sm, __ldg(c.src + base + lane)) : 0.0f;
     scratch[lane] = e;
     __syncwarp();
@@ -347,6 +355,53 @@ __device__ __forceinline__ void load_chunk(const Ctx& c, int t, float (&a)[kSC])
     }
 }
 
+
+// x = l/T for the rows the kernel takes (see the lean-row rule in the kernel).
+__device__ __forceinline__ float div_lean(float l, const Ctx& c) {
+    const float q = __fmul_rn(l, c.rT);
+    const float r = __fmaf_rn(-q, c.T, l);
+    return __fmaf_rn(r, c.rT, q);
+}
+
+// Pass 2 over one chunk: exact e = exp(l/T - max) unless absorbed (d <
+// d_thr), the chain sums in the primary (v0, v1) and alternative (w0, w1)
+// binade, candidate counts in the histogram, and the values of kept chunks.
+// kGeneral: a partial chunk, or one whose threshold reaches below the fast
+// exp range (its d may need the out-of-range exp).
+template <bool kGeneral>
+__device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx& c, StreamSmem& sm, float d_thr,
+                                            float e_min, float* keep, float& v0, float& v1, float& w0, float& w1) {
+    // three granules in flight: rotate qa <- qb <- qc <- load(g + 3)
+    float4 qa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), qb = qa, qc = qa;
+    if (!kGeneral || 0 < cnt) qa = ldg4(cp);
+    if (!kGeneral || 4 < cnt) qb = ldg4(cp + 4);
+    if (!kGeneral || 8 < cnt) qc = ldg4(cp + 8);
+#pragma unroll 1
+    for (int g = 0; g < kSC / 4; ++g) {
+        float4 qn = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (4 * (g + 3) < (kGeneral ? cnt : kSC)) qn = ldg4(cp + 4 * (g + 3));
+        float a[4] = {qa.x, qa.y, qa.z, qa.w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            float e = 0.0f;
+            if (!kGeneral || 4 * g + w < cnt) {
+                const float d = __fsub_rn(div_lean(a[w], c), c.max_x);
+                if (!(d < d_thr)) e = kGeneral ? xm::exp_f32(d, sm.exptab) : xm::exp_normal_range(d, sm.exptab);
+                if (e >= e_min) atomicAdd(&sm.hist[bin_of(e)], 1);
+            }
+            a[w] = e;
+            v0 = __fadd_rn(v0, e);
+            v1 = __fadd_rn(v1, e);
+            w0 = __fadd_rn(w0, e);
+            w1 = __fadd_rn(w1, e);
+        }
+        if (keep) reinterpret_cast<float4*>(keep)[g] = make_float4(a[0], a[1], a[2], a[3]);
+        qa = qb;
+        qb = qc;
+        qc = qn;
+    }
+}
+
 __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     StreamSmem& sm = *reinterpret_cast<StreamSmem*>(smem_raw);
@@ -355,8 +410,7 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
     __syncthreads();
     const int V = p.vocab;
     const int nch = (V + kSC - 1) / kSC;
-    // per-CTA L2-resident scratch: the candidate list, then (for nuclei above
-    // the on-chip capacity) the sorted nucleus
+    // per-CTA L2-resident scratch for nuclei above the on-chip capacity
     unsigned long long* super = p.workspace + (long long)blockIdx.x * p.ws_stride;
 
     for (int row = blockIdx.x; row < p.batch; row += gridDim.x) {
@@ -426,22 +480,30 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
         for (int sidx = 0; sidx < kStrips; ++sidx) {
             const int t = sidx * kST + tid;
             float m2 = -3.4e38f, s2 = 0.0f;
-            const int cnt = (t < nch) ? min(kSC, V - t * kSC) : 0;
-            const float* cp = c.src + t * kSC;
-#pragma unroll 2
-            for (int g = 0; g < cnt; g += 4) {
-                const float4 q = ldg4(cp + g);
-                const float a[4] = {q.x, q.y, q.z, q.w};
+            if (t < nch) {
+                float a[kSC];
+                load_chunk(c, t, a);  // eight loads in flight
+                const int cnt = min(kSC, V - t * kSC);
+                if (cnt == kSC) {
 #pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    mxl = fmaxf(mxl, a[w]);
-                    mnl = fminf(mnl, a[w]);
-                    const float xs = a[w] * k2;
-                    if (xs > m2) {
-                        s2 = s2 * ex2_approx(m2 - xs);
-                        m2 = xs;
+                    for (int j = 0; j < kSC; ++j) {
+                        mxl = fmaxf(mxl, a[j]);
+                        mnl = fminf(mnl, a[j]);
+                        m2 = fmaxf(m2, a[j] * k2);
                     }
-                    s2 += ex2_approx(xs - m2);
+#pragma unroll
+                    for (int j = 0; j < kSC; ++j) s2 += ex2_approx(__fmaf_rn(a[j], k2, -m2));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kSC; ++j)
+                        if (j < cnt) {
+                            mxl = fmaxf(mxl, a[j]);
+                            mnl = fminf(mnl, a[j]);
+                            m2 = fmaxf(m2, a[j] * k2);
+                        }
+#pragma unroll
+                    for (int j = 0; j < kSC; ++j)
+                        if (j < cnt) s2 += ex2_approx(__fmaf_rn(a[j], k2, -m2));
                 }
             }
             cm2[sidx] = m2;
@@ -461,7 +523,6 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
             sm.red_c[warp] = wm2;
         }
         if (tid == 0) {
-            sm.n_super = 0;
             sm.n_alt = 0;
             sm.n_side = 0;
             sm.flag = 0;
@@ -478,6 +539,21 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
         }
         __syncthreads();  // red_* are reused by the scans below
         c.max_x = c.unit ? MX : (c.T > 0.0f ? __fdiv_rn(MX, c.T) : __fdiv_rn(MN, c.T));
+        // Rows this kernel takes: x = l/T by the unguarded Markstein division,
+        // correctly rounded for |T| in [2^-10, 2^10] and |l| in [2^-60, 2^60]
+        // (and for l = 0).  A nonzero |l| < 2^-60 gives |x| < 2^-49, below
+        // half an ulp of max_x when |max_x| >= 2^-24, so d = fl(x - max_x) =
+        // -max_x whatever the quotient's last bits.  Other rows (huge logits,
+        // extreme temperatures, a tiny row maximum) go to the general kernel.
+        {
+            const float aT = fabsf(c.T);
+            const bool lean = aT >= 0x1p-10f && aT <= 0x1p10f && fmaxf(fabsf(MX), fabsf(MN)) <= 0x1p60f &&
+                              fabsf(c.max_x) >= 0x1p-24f;
+            if (!lean) {
+                if (tid == 0) defer_row_s(p, row);
+                continue;
+            }
+        }
         // approximate chunk sums in units of exp(x - max); exclusive prefix in
         // chunk order (strip-major)
         float sig[kStrips], gss[kStrips];
@@ -491,7 +567,7 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
         }
         const float s_approx = strip_off;
 
-        // ---- pass 2: exact e where it matters, chunk functions, candidates
+        // ---- pass 2: exact e where it matters, chunk functions, histogram
         const float cutoff = __fdiv_rn(__fsub_rn(1.0f, topp), (float)(V - 1));  // llama2.c:1024
         const float e_min = cutoff * s_approx * 0.9921875f;
         const float d_cand = (e_min > 0.0f) ? __logf(e_min) - 1e-3f : -INFINITY;
@@ -522,50 +598,11 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
             const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
             float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
             const float* cp = c.src + t * kSC;
-#pragma unroll 1
-            for (int g = 0; g < kSC / 4; ++g) {
-                float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (4 * g < cnt) q = ldg4(cp + 4 * g);
-                float a[4] = {q.x, q.y, q.z, q.w};
-                unsigned cm = 0u;
-#pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    float e = 0.0f;
-                    if (4 * g + w < cnt) {
-                        const float x = c.unit ? a[w] : xm_div_const(a[w], c.T, c.rT);
-                        const float d = __fsub_rn(x, c.max_x);
-                        if (!(d < d_thr)) e = xm::exp_f32(d, sm.exptab);
-                        nan_any |= isnan(e);
-                        if (e >= e_min && !isnan(e)) cm |= 1u << w;
-                    }
-                    a[w] = e;
-                    v0 = __fadd_rn(v0, e);
-                    v1 = __fadd_rn(v1, e);
-                    w0 = __fadd_rn(w0, e);
-                    w1 = __fadd_rn(w1, e);
-                }
-                if (keep) reinterpret_cast<float4*>(keep)[g] = make_float4(a[0], a[1], a[2], a[3]);
-                // top-p candidates of this granule, one atomic per warp
-                if (__any_sync(kFullMask, cm != 0u)) {
-                    const int my = __popc(cm);
-                    int incl = my;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const int y = __shfl_up_sync(kFullMask, incl, o);
-                        if (lane >= o) incl += y;
-                    }
-                    int b0 = 0;
-                    if (lane == 31) b0 = atomicAdd(&sm.n_super, incl);
-                    b0 = __shfl_sync(kFullMask, b0, 31) + incl - my;
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        if (cm & (1u << w)) {
-                            super[b0++] = cand_key(a[w], t * kSC + 4 * g + w);
-                            atomicAdd(&sm.hist[bin_of(a[w])], 1);
-                        }
-                    }
-                }
-            }
+            if (cnt == kSC && d_thr >= xm::kExpFastMin)
+                pass2_chunk<false>(cp, cnt, c, sm, d_thr, e_min, keep, v0, v1, w0, w1);
+            else if (valid)
+                pass2_chunk<true>(cp, cnt, c, sm, d_thr, e_min, keep, v0, v1, w0, w1);
+            nan_any |= isnan(v0);  // a NaN e propagates into every chain sum
             // chunk functions (primary and alternative binade)
             const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
             const bool aclean = valid && alt != 0u && (__float_as_uint(w0) >> 23) == alt && (__float_as_uint(w1) >> 23) == alt;
@@ -609,16 +646,12 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
         if (row_nan) {
             flags = kFlagNan | kFlagNoCand;
         } else {
-            // ---- exact S
-            if (warp == 0) {
-                const float S = resolve_S(sm, c);
-                if (lane == 0) sm.fval = S;
-            }
-            __syncthreads();
-            const float S = sm.fval;
-            // ---- nucleus selection: guaranteed mass of bins 0..D
+            // ---- nucleus bins from the histogram: guaranteed mass of bins 0..D
+            // against topp plus the fp32 drift bound, with the approximate S
+            // scaled up by the 2^-7 margin that bounds its distance to the
+            // exact serial S (checked after the walk: a miss defers the row)
             int h[kBinsPerThread];
-            int hc = 0, nsort = 0;
+            int hc = 0;
             float hm = 0.0f;
 #pragma unroll
             for (int q = 0; q < kBinsPerThread; ++q) {
@@ -630,7 +663,7 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
             const ScanF ms = block_scan_f(hm, sm);
             int ctot;
             const int cex = block_scan_i(hc, sm, ctot) - hc;
-            const float target = (topp + 4096.0f * 0x1p-24f + 1e-5f) * S * 1.0000005f;
+            const float target = (topp + 4096.0f * 0x1p-24f + 1e-5f) * s_approx * 1.0078125f;
             if (ms.incl >= target && ms.excl < target) {
                 float m = ms.excl;
                 int cc = cex, d = tid * kBinsPerThread + kBinsPerThread - 1;
@@ -653,14 +686,11 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                 D = kBins - 1;
                 K = ctot;
             }
-            const int nsup = sm.n_super;
-            // the nucleus lives on chip, or after the candidate list in L2
-            unsigned long long* kb = (K <= kKCap) ? sm.kbuf : super + ((nsup + 1) & ~1);
-            if (K > 4096) {  // beyond the drift bound the selection margin covers
-                defer = true;
-            } else {
-                // bin offsets (hist becomes the scatter cursor) and the list of
-                // bins that need sorting (kept in the side area)
+            // the nucleus lives on chip, or in the CTA's L2 scratch
+            unsigned long long* kb = (K <= kKCap) ? sm.kbuf : super;
+            const bool fits = K <= 4096;
+            if (fits) {
+                // bin offsets (hist becomes the scatter cursor)
                 int run = cex;
 #pragma unroll
                 for (int q = 0; q < kBinsPerThread; ++q) {
@@ -669,107 +699,156 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                         sm.bstart[b] = (short)run;
                         sm.hist[b] = run;
                         run += h[q];
-                        nsort += (h[q] >= 2) ? 1 : 0;
                     }
                 }
-                int nlist;
-                int wpos = block_scan_i(nsort, sm, nlist) - nsort;
-                int* list = reinterpret_cast<int*>(&sm.side[0][0]);
+            }
+            __syncthreads();
+            if (warp == 0) {
+                // ---- exact S (overlaps the extraction below)
+                const float S = resolve_S(sm, c);
+                if (lane == 0) sm.fval = S;
+            } else if (fits) {
+                // ---- re-read the row (L2) and place the elements of bins
+                // 0..D, then sort each bin by (e desc, index asc)
+                // Logit-space pre-filter: every element of bins 0..D has
+                // e >= e_x = max(lower edge of bin D, e_min), so d >= ln(e_x) -
+                // eps; d = fl(fl(l/T) - max) is monotone in l, and l beyond
+                // l_lo (T > 0: below; T < 0: above) by a relative 2^-20 plus
+                // the absolute 1e-3 margin cannot be one of them.
+                const float e_x = fmaxf(bin_lo(D), e_min);
+                const float d_x = (e_x > 0.0f) ? __logf(e_x) - 1e-3f : -INFINITY;
+                const float tl = __fmul_rn(c.T, __fadd_rn(c.max_x, d_x));
+                const float l_lo = (c.T > 0.0f) ? (tl - fabsf(tl) * 0x1p-20f - fabsf(c.T) * 5e-4f)
+                                                : (tl + fabsf(tl) * 0x1p-20f + fabsf(c.T) * 5e-4f);
+                const float sg = (c.T > 0.0f) ? 1.0f : -1.0f;
+                const float l_cmp = sg * l_lo;
+                const int u = tid - 32, nu = kST - 32;
+                const float4* row4 = reinterpret_cast<const float4*>(c.src);
+                const int ng = V / 4;
+                for (int g0 = u; g0 < ng; g0 += 4 * nu) {
+                    float4 q[4];
 #pragma unroll
-                for (int q = 0; q < kBinsPerThread; ++q) {
-                    const int b = tid * kBinsPerThread + q;
-                    if (b <= D && h[q] >= 2) list[wpos++] = b;
-                }
-                for (int i = tid; i < nsup; i += kST) {
-                    const unsigned long long k = super[i];
-                    const int b = bin_of(key_prob(k));
-                    if (b <= D) {
-                        const int pos = atomicAdd(&sm.hist[b], 1);
-                        if (pos < K) kb[pos] = k;
+                    for (int k = 0; k < 4; ++k)
+                        q[k] = (g0 + k * nu < ng) ? __ldg(row4 + g0 + k * nu)
+                                                  : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                    uint32_t m = 0u;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        m |= (sg * q[k].x < l_cmp) ? 0u : (1u << (4 * k));
+                        m |= (sg * q[k].y < l_cmp) ? 0u : (2u << (4 * k));
+                        m |= (sg * q[k].z < l_cmp) ? 0u : (4u << (4 * k));
+                        m |= (sg * q[k].w < l_cmp) ? 0u : (8u << (4 * k));
                     }
-                }
-                if (tid == 0) sm.flag = 0;
-                __syncthreads();
-                // sort each bin by (e desc, index asc)
-                for (int q = warp; q < nlist; q += kSW) {
-                    const int b = list[q];
-                    const int s0 = sm.bstart[b];
-                    const int n = sm.hist[b] - s0;
-                    if (s0 < 0 || s0 + n > K) {
-                        if (lane == 0) sm.flag = 1;
-                        continue;
-                    }
-                    unsigned long long* seg = kb + s0;
-                    if (n <= 32) warp_sort_desc<1>(seg, n, lane);
-                    else if (n <= 64) warp_sort_desc<2>(seg, n, lane);
-                    else if (n <= 128) warp_sort_desc<4>(seg, n, lane);
-                    else if (n <= 256) warp_sort_desc<8>(seg, n, lane);
-                    else if (lane == 0) sm.flag = 1;
-                }
-                __syncthreads();
-                if (sm.flag) {
-                    defer = true;
-                } else {
-                    // p = fl(e/S) in place of e; flag equal-p runs out of index order
-                    bool bad = false;
-                    for (int i = tid; i < K; i += kST) {
-                        const unsigned long long k = kb[i];
-                        const float pv = __fdiv_rn(key_prob(k), S);
-                        kb[i] = ((unsigned long long)__float_as_uint(pv) << 32) | (k & 0xFFFFFFFFull);
-                    }
-                    __syncthreads();
-                    for (int i = tid; i + 1 < K; i += kST) {
-                        const unsigned long long a = kb[i], b = kb[i + 1];
-                        bad |= ((a >> 32) == (b >> 32)) && (key_index(a) > key_index(b));
-                    }
-                    if (__syncthreads_or(bad) && tid == 0) {
-                        for (bool swapped = true; swapped;) {
-                            swapped = false;
-                            for (int i = 0; i + 1 < K; ++i) {
-                                const unsigned long long a = kb[i], b = kb[i + 1];
-                                if ((a >> 32) == (b >> 32) && key_index(a) > key_index(b)) {
-                                    kb[i] = b;
-                                    kb[i + 1] = a;
-                                    swapped = true;
+                    // padding (-inf * sg) never passes for T > 0; for T < 0 it
+                    // is excluded by the granule bound below
+                    while (m) {
+                        const int j = __ffs(m) - 1;
+                        m &= m - 1;
+                        const int gi = g0 + (j >> 2) * nu;
+                        if (gi >= ng) continue;
+                        const int idx = 4 * gi + (j & 3);
+                        const float d = __fsub_rn(div_lean(__ldg(c.src + idx), c), c.max_x);
+                        if (d >= d_cand) {
+                            const float e = xm::exp_f32(d, sm.exptab);
+                            if (e >= e_min) {
+                                const int b = bin_of(e);
+                                if (b <= D) {
+                                    const int pos = atomicAdd(&sm.hist[b], 1);
+                                    if (pos < K) kb[pos] = cand_key(e, idx);
                                 }
                             }
                         }
                     }
-                    __syncthreads();
-                    // candidates proper (p >= cutoff) form a prefix
-                    int n0loc = 0;
-                    for (int i = tid; i < K; i += kST) n0loc += (key_prob(kb[i]) >= cutoff) ? 1 : 0;
-                    int n0;
-                    block_scan_i(n0loc, sm, n0);
-                    if (warp == 0) {
-                        int res = -1;
-                        if (n0 == 0) {
-                            res = all_cand ? -2 : -1;
-                        } else {
-                            auto get = [&](int i) { return key_prob(kb[i]); };
-                            float cum = 0.0f;
-                            int last = warp_chain(get, n0, cum, topp);  // llama2.c:1036-1043
-                            if (last >= n0) last = all_cand ? n0 - 1 : -1;  // llama2.c:1037
-                            if (last >= 0) {
-                                const float r = __fmul_rn(coin, cum);  // llama2.c:1046
-                                float s3 = 0.0f;
-                                int k = warp_chain(get, last + 1, s3, r);
-                                if (k > last) k = last;  // llama2.c:1055
-                                res = key_index(kb[k]);
+                }
+                named_bar(1, kST - 32);
+                // sort the bins holding two or more elements: warp w takes
+                // the groups of 32 bins w-1, w-1+7, ...
+                for (int b0 = (warp - 1) * 32; b0 <= D; b0 += (kSW - 1) * 32) {
+                    const int b = b0 + lane;
+                    int s0 = 0, n = 0;
+                    if (b <= D) {
+                        s0 = sm.bstart[b];
+                        n = sm.hist[b] - s0;
+                        if (s0 < 0 || s0 + n > K || n > 256) sm.flag = 1;
+                    }
+                    unsigned todo = __ballot_sync(kFullMask, n >= 2 && n <= 256 && s0 >= 0 && s0 + n <= K);
+                    while (todo) {
+                        const int src = __ffs(todo) - 1;
+                        todo &= todo - 1;
+                        const int ss = __shfl_sync(kFullMask, s0, src);
+                        const int nn = __shfl_sync(kFullMask, n, src);
+                        unsigned long long* seg = kb + ss;
+                        if (nn <= 32) warp_sort_desc<1>(seg, nn, lane);
+                        else if (nn <= 64) warp_sort_desc<2>(seg, nn, lane);
+                        else if (nn <= 128) warp_sort_desc<4>(seg, nn, lane);
+                        else warp_sort_desc<8>(seg, nn, lane);
+                    }
+                }
+            }
+            __syncthreads();
+            const float S = sm.fval;
+            if (!fits || sm.flag) {
+                defer = true;
+            } else {
+                // p = fl(e/S) in place of e; flag equal-p runs out of index order
+                bool bad = false;
+                for (int i = tid; i < K; i += kST) {
+                    const unsigned long long k = kb[i];
+                    const float pv = __fdiv_rn(key_prob(k), S);
+                    kb[i] = ((unsigned long long)__float_as_uint(pv) << 32) | (k & 0xFFFFFFFFull);
+                }
+                __syncthreads();
+                for (int i = tid; i + 1 < K; i += kST) {
+                    const unsigned long long a = kb[i], b = kb[i + 1];
+                    bad |= ((a >> 32) == (b >> 32)) && (key_index(a) > key_index(b));
+                }
+                if (__syncthreads_or(bad) && tid == 0) {
+                    for (bool swapped = true; swapped;) {
+                        swapped = false;
+                        for (int i = 0; i + 1 < K; ++i) {
+                            const unsigned long long a = kb[i], b = kb[i + 1];
+                            if ((a >> 32) == (b >> 32) && key_index(a) > key_index(b)) {
+                                kb[i] = b;
+                                kb[i + 1] = a;
+                                swapped = true;
                             }
                         }
-                        if (lane == 0) sm.result = res;
                     }
-                    __syncthreads();
-                    const int res = sm.result;
-                    if (res == -1) {
-                        defer = true;
-                    } else if (res == -2) {
-                        flags |= kFlagNoCand;
-                        id = 0;
+                }
+                __syncthreads();
+                // candidates proper (p >= cutoff) form a prefix
+                int n0loc = 0;
+                for (int i = tid; i < K; i += kST) n0loc += (key_prob(kb[i]) >= cutoff) ? 1 : 0;
+                int n0;
+                block_scan_i(n0loc, sm, n0);
+                if (warp == 0) {
+                    int res = -1;
+                    if (n0 == 0) {
+                        res = all_cand ? -2 : -1;
                     } else {
-                        id = res;
+                        auto get = [&](int i) { return key_prob(kb[i]); };
+                        float cum = 0.0f;
+                        int last = warp_chain(get, n0, cum, topp);  // llama2.c:1036-1043
+                        if (last >= n0) last = all_cand ? n0 - 1 : -1;  // llama2.c:1037
+                        if (last >= 0) {
+                            const float r = __fmul_rn(coin, cum);  // llama2.c:1046
+                            float s3 = 0.0f;
+                            int k = warp_chain(get, last + 1, s3, r);
+                            if (k > last) k = last;  // llama2.c:1055
+                            res = key_index(kb[k]);
+                        }
                     }
+                    if (lane == 0) sm.result = res;
+                }
+                __syncthreads();
+                const int res = sm.result;
+                if (res == -1) {
+                    defer = true;
+                } else if (res == -2) {
+                    flags |= kFlagNoCand;
+                    id = 0;
+                } else {
+                    id = res;
                 }
             }
         }
