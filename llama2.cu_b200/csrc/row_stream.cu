@@ -363,14 +363,15 @@ __device__ __forceinline__ float div_lean(float l, const Ctx& c) {
     return __fmaf_rn(r, c.rT, q);
 }
 
-// Pass 2 over one chunk: exact e = exp(l/T - max) unless absorbed (d <
-// d_thr), the chain sums in the primary (v0, v1) and alternative (w0, w1)
-// binade, candidate counts in the histogram, and the values of kept chunks.
-// kGeneral: a partial chunk, or one whose threshold reaches below the fast
-// exp range (its d may need the out-of-range exp).
+// Pass 2 over one chunk: exact e = exp(l/T - max) of every element (a
+// per-element skip of the values the serial sum absorbs costs more in
+// divergence than the exp it saves), the chain sums in the primary (v0, v1)
+// and alternative (w0, w1) binade, candidate counts in the histogram, and the
+// values of kept chunks.  kGeneral: a partial chunk, or a row whose d range
+// reaches below the fast exp range.
 template <bool kGeneral>
-__device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx& c, StreamSmem& sm, float d_thr,
-                                            float e_min, float* keep, float& v0, float& v1, float& w0, float& w1) {
+__device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx& c, StreamSmem& sm, float e_min,
+                                            float* keep, float& v0, float& v1, float& w0, float& w1) {
     // three granules in flight: rotate qa <- qb <- qc <- load(g + 3)
     float4 qa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), qb = qa, qc = qa;
     if (!kGeneral || 0 < cnt) qa = ldg4(cp);
@@ -386,7 +387,7 @@ __device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx&
             float e = 0.0f;
             if (!kGeneral || 4 * g + w < cnt) {
                 const float d = __fsub_rn(div_lean(a[w], c), c.max_x);
-                if (!(d < d_thr)) e = kGeneral ? xm::exp_f32(d, sm.exptab) : xm::exp_normal_range(d, sm.exptab);
+                e = kGeneral ? xm::exp_f32(d, sm.exptab) : xm::exp_normal_range(d, sm.exptab);
                 if (e >= e_min) atomicAdd(&sm.hist[bin_of(e)], 1);
             }
             a[w] = e;
@@ -571,22 +572,24 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
         const float cutoff = __fdiv_rn(__fsub_rn(1.0f, topp), (float)(V - 1));  // llama2.c:1024
         const float e_min = cutoff * s_approx * 0.9921875f;
         const float d_cand = (e_min > 0.0f) ? __logf(e_min) - 1e-3f : -INFINITY;
+        // every d = fl(x - max) lies in [fl(min_x - max_x), 0]: rows whose
+        // range stays inside the fast exp range skip the range check
+        const float min_x = c.unit ? MN : (c.T > 0.0f ? __fdiv_rn(MN, c.T) : __fdiv_rn(MX, c.T));
+        const bool wide = !(__fsub_rn(min_x, c.max_x) >= xm::kExpFastMin);
+        // a NaN logit makes the approximate sum NaN (ex2.approx(NaN) = NaN),
+        // and the reference's softmax then yields all-NaN probabilities: such
+        // rows skip pass 2 (whose fast exp does not carry NaN through)
+        const bool nan_row = isnan(s_approx);
         bool nan_any = false;
 #pragma unroll 1
-        for (int sidx = 0; sidx < kStrips; ++sidx) {
+        for (int sidx = 0; sidx < (nan_row ? 0 : kStrips); ++sidx) {
             const int t = sidx * kST + tid;
             const bool valid = t < nch;
             const int cnt = valid ? min(kSC, V - t * kSC) : 0;
             uint32_t alt = 0u;
             const uint32_t eb = valid ? xm::chain_guess_primary(gss[sidx], sig[sidx], alt) : 0u;
-            // e is absorbed when below half an ulp of a running sum in binade
-            // tb (exp(d) < 2^(tb-151)); never for a possible candidate
-            const uint32_t tb = (eb == 0u) ? 0u : ((alt != 0u && alt < eb) ? alt : eb);
-            const float d_abs = (tb == 0u) ? -INFINITY : ((float)((int)tb - 151) * 0.69314718f - 1e-4f);
-            const float d_thr = fminf(d_abs, d_cand);
             // chunks whose binade is unknown or near a boundary keep their
-            // values for a possible serial replay (absorbed ones are exact zeros
-            // in every binade at or above tb)
+            // values for a possible serial replay
             float* keep = nullptr;
             int keep_idx = -1;
             if (valid && (eb == 0u || alt != 0u)) {
@@ -598,11 +601,11 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
             const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
             float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
             const float* cp = c.src + t * kSC;
-            if (cnt == kSC && d_thr >= xm::kExpFastMin)
-                pass2_chunk<false>(cp, cnt, c, sm, d_thr, e_min, keep, v0, v1, w0, w1);
+            if (cnt == kSC && !wide)
+                pass2_chunk<false>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
             else if (valid)
-                pass2_chunk<true>(cp, cnt, c, sm, d_thr, e_min, keep, v0, v1, w0, w1);
-            nan_any |= isnan(v0);  // a NaN e propagates into every chain sum
+                pass2_chunk<true>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
+            nan_any |= isnan(v0);
             // chunk functions (primary and alternative binade)
             const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
             const bool aclean = valid && alt != 0u && (__float_as_uint(w0) >> 23) == alt && (__float_as_uint(w1) >> 23) == alt;
@@ -630,7 +633,7 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                 sm.wfn[sidx * kSW + warp] =
                     make_float4(F.L0, F.L1, __uint_as_float(F.pbits | (uni ? kFClean : 0u)), __uint_as_float(eb0));
         }
-        const bool row_nan = __syncthreads_or(nan_any) != 0;
+        const bool row_nan = (__syncthreads_or(nan_any) != 0) || nan_row;
 
         // ---- coin (drawn before the walk, llama2.c:1094); state committed at the end
         unsigned long long st = 0;

@@ -275,7 +275,19 @@ EDGE = [
 EDGE_CASES_FAST = EDGE + [
     ("nan_in_topp_row", lambda r: np.tile(np.array([1.0, np.nan] + [0.5] * 30, np.float32), (r, 1)), 1.0, 0.9),
     ("one_hot", lambda r: np.where(np.arange(32000) == 777, 30.0, 0.0).astype(np.float32)[None, :].repeat(r, 0), 1.0, 0.9),
+    ("nan_first_wide", lambda r: _with(np.random.default_rng(16).normal(0, 2, (r, 32000)), [0], np.nan), 0.8, 0.9),
+    ("nan_middle_wide", lambda r: _with(np.random.default_rng(17).normal(0, 2, (r, 32000)), [20001], np.nan), 0.8, 0.9),
+    ("wide_spread", lambda r: np.random.default_rng(18).normal(0, 30, (r, 32000)).astype(np.float32), 0.7, 0.9),
+    ("tiny_logits", lambda r: np.random.default_rng(19).normal(0, 1e-30, (r, 32000)).astype(np.float32), 1.0, 0.9),
+    ("some_tiny_logits", lambda r: _with(np.random.default_rng(20).normal(0, 2, (r, 32000)), list(range(0, 32000, 97)),
+                                         1e-30), 0.7, 0.9),
 ]
+
+
+def _with(x, cols, value):
+    x = x.astype(np.float32)
+    x[:, cols] = value
+    return x
 
 
 @pytest.mark.parametrize("name,make,temp,topp", EDGE)
