@@ -152,6 +152,25 @@ int sampler_last_launch_count(void);
 /* Human-readable text of the last error on this thread. */
 const char* sampler_last_error(void);
 
+/* Fused variant: the classifier projection and the sampling of its rows.
+ * Replaces, per decode step, the classifier matmul of the final hidden state
+ * (llama2_cublas.cu:5825-5826 cublasSgemv with wcls; the bf16 GemmEx form
+ * llama2_cublas_bf16.cu:411) followed by sample() on the host
+ * (llama2_cublas.cu:5831-5905), for `batch` rows at once:
+ *   logits[b, v] = sum_k hidden[b, k] * wcls[v, k]   (bf16 in, fp32 accumulate)
+ * on the sm_100a tensor cores, whose epilogue also emits the per-row softmax
+ * statistics the sampler needs, then per row exactly what sampler_batched()
+ * does on those logits (same ids, states and flags).
+ *   hidden     bf16 [batch, dim] row-major (16-byte aligned), dim % 8 == 0
+ *   wcls       bf16 [vocab_size, dim] row-major (16-byte aligned)
+ *   cfg        vocab_size % 32 == 0, <= SAMPLER_MAX_VOCAB; flags must be 0
+ *   logits_out fp32 [batch, vocab_size] or NULL (then library-managed)
+ * Other arguments as in sampler_batched().  Asynchronous on `stream`. */
+int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, const void* wcls, int batch,
+                            int dim, const float* temperature_rows, const float* topp_rows, const float* coins,
+                            unsigned long long* rng_state, int* out_ids, float* logits_out, int* row_flags,
+                            void* stream);
+
 /* Largest vocabulary sampler_batched_noalloc accepts. */
 #define SAMPLER_NOALLOC_MAX_VOCAB 32768
 

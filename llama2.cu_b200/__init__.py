@@ -22,7 +22,7 @@ EXPORTED_SYMBOLS = [
     "sample_topp", "sample", "sampler_workspace_bytes", "sampler_batched", "sampler_batched_host",
     "sampler_seed_states", "sampler_last_launch_count", "sampler_last_error", "sampler_shard_rows",
     "sampler_nccl_get_unique_id", "sampler_nccl_comm_init", "sampler_nccl_allgather_ids",
-    "sampler_nccl_comm_destroy", "sampler_batched_noalloc",
+    "sampler_nccl_comm_destroy", "sampler_batched_noalloc", "classifier_sample_fused",
 ]
 
 
@@ -102,6 +102,9 @@ def lib():
     L.sampler_nccl_allgather_ids.restype = c_int
     L.sampler_nccl_comm_destroy.argtypes = [P]
     L.sampler_nccl_comm_destroy.restype = c_int
+    L.classifier_sample_fused.argtypes = [ctypes.POINTER(SamplerBatchConfig), P, P, c_int, c_int, P, P, P, P, P, P,
+                                          P, P]
+    L.classifier_sample_fused.restype = c_int
     _lib = L
     return L
 
@@ -162,6 +165,34 @@ def sample_batched(logits, temperature, topp, rng_state=None, *, temperature_row
                                _ptr(topp_rows), _ptr(coins), _ptr(rng_state), _ptr(out_ids), _ptr(probs_out),
                                _ptr(row_flags), _ptr(workspace), ws_bytes, _stream_ptr(stream))
     _check(rc, "sampler_batched")
+    return out_ids
+
+
+def classifier_sample_fused(hidden, wcls, temperature, topp, rng_state=None, *, temperature_rows=None,
+                            topp_rows=None, coins=None, out_ids=None, logits_out=None, row_flags=None, stream=None):
+    """Fused classifier + sampling: hidden bf16 CUDA [B, D], wcls bf16 CUDA
+    [V, D]; logits = hidden . wcls^T (fp32, optionally returned in
+    logits_out [B, V]) sampled per row as sample_batched() does.
+    Returns out_ids (int32 CUDA tensor [B]).  Asynchronous on `stream`."""
+    import torch
+    _require_cuda(hidden, wcls, rng_state, temperature_rows, topp_rows, coins, logits_out, row_flags)
+    for t in (hidden, wcls):
+        if t.dtype != torch.bfloat16 or t.dim() != 2 or not t.is_contiguous():
+            raise SamplerError("hidden and wcls must be contiguous bfloat16 matrices")
+    B, D = hidden.shape
+    V = wcls.shape[0]
+    if wcls.shape[1] != D:
+        raise SamplerError("hidden and wcls disagree on the model dimension")
+    if logits_out is not None and (logits_out.dtype != torch.float32 or tuple(logits_out.shape) != (B, V)
+                                   or not logits_out.is_contiguous()):
+        raise SamplerError("logits_out must be a contiguous float32 [B, V] tensor")
+    if out_ids is None:
+        out_ids = torch.empty(B, dtype=torch.int32, device=hidden.device)
+    cfg = SamplerBatchConfig(V, float(temperature), float(topp), 0)
+    rc = lib().classifier_sample_fused(ctypes.byref(cfg), _ptr(hidden), _ptr(wcls), B, D, _ptr(temperature_rows),
+                                       _ptr(topp_rows), _ptr(coins), _ptr(rng_state), _ptr(out_ids),
+                                       _ptr(logits_out), _ptr(row_flags), _stream_ptr(stream))
+    _check(rc, "classifier_sample_fused")
     return out_ids
 
 

@@ -11,7 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libb200_sampler.so")
-SOURCES = ["sampler_kernels.cu", "row_stream.cu", "sampler_api.cu", "noalloc.cu"]
+SOURCES = ["sampler_kernels.cu", "row_stream.cu", "classifier_gemm.cu", "sampler_api.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1,0 +1,376 @@
+// classifier_gemm.cu -- the classifier projection of the fused variant:
+// logits[B, V] = H[B, D] . Wcls[V, D]^T in bf16 with fp32 accumulation, on
+// the 5th-generation tensor cores (tcgen05.mma, accumulator in TMEM), with
+// an epilogue that also emits the per-chunk statistics the streaming sampler
+// would otherwise compute in its first pass over the logits.
+//
+// It replaces the reference's classifier matmul followed by the host sampler
+// (llama2_cublas.cu:5825-5826 cublasSgemv of wcls, llama2_cublas_bf16.cu:411
+// the bf16 GemmEx form), at batch B instead of one token.
+//
+// Persistent kernel, one 256-thread CTA per SM, tile 128 (rows of H) x 256
+// (vocabulary entries), K step 64:
+//   warp 0     TMA producer: A [128 x 64] and B [256 x 64] bf16 boxes, 128-byte
+//              swizzle, into a 4-stage ring (48 KB a stage)
+//   warp 1     MMA issuer (one thread): four tcgen05.mma (M128 N256 K16) per
+//              stage, tcgen05.commit releases the stage; the accumulator is
+//              double-buffered in TMEM (2 x 256 columns)
+//   warp 2     TMEM allocation / release
+//   warps 4-7  epilogue: tcgen05.ld of 32 columns at a time (one row per
+//              thread), fp32 logits to HBM and, per 32-column chunk, the
+//              statistics (max, min, approximate sum of exp((l - max)/T))
+// No cluster, no multicast: every CTA loads its own tiles (the kernel also
+// runs on every GPU of a multi-GPU job).  Every mbarrier wait is bounded; a
+// timeout sets the error word and drains the pipeline.
+#include "device_common.cuh"
+#include "sampler_kernels.cuh"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <mutex>
+
+namespace b2s {
+namespace {
+
+constexpr int kGM = 128;      // rows of H per tile (TMEM lanes)
+constexpr int kGN = 256;      // vocabulary entries per tile (TMEM columns)
+constexpr int kGK = 64;       // K per stage: 128 bytes of bf16, one swizzle span
+constexpr int kStages = 4;
+constexpr int kGThreads = 256;
+constexpr int kABytes = kGM * kGK * 2;  // 16 KB
+constexpr int kBBytes = kGN * kGK * 2;  // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kTmemCols = 2 * kGN;      // two accumulators
+constexpr int kGroupM = 16;             // M blocks swept together (L2 reuse of W)
+
+struct GemmSmem {
+    uint8_t a[kStages][kABytes];  // 1024-byte aligned (the swizzle atom)
+    uint8_t b[kStages][kBBytes];
+    unsigned long long full[kStages];
+    unsigned long long empty[kStages];
+    unsigned long long tmem_full[2];
+    unsigned long long tmem_empty[2];
+    unsigned long long drain;
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr size_t kGemmSmemBytes = sizeof(GemmSmem) + 1024;  // + alignment slack
+
+// ---- tcgen05 wrappers ------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, kind::f16 (bf16 inputs, fp32 accumulator)
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives on `bar` once every tcgen05 operation this thread issued so far is done.
+__device__ __forceinline__ void tc_commit(unsigned long long* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile stored as rows of
+// 128 bytes with the 128-byte swizzle (the layout TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B): start address >> 4 in bits 0-13, leading
+// byte offset (unused for swizzled K-major; 1) in 16-29, stride byte offset
+// between 8-row groups (1024 B) >> 4 in 32-45, descriptor version 1 in
+// 46-47, swizzle mode 2 (128 B) in 61-63.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)1u << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and
+// B bf16 (bits 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0),
+// N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGN >> 3) << 17) |
+                            ((uint32_t)(kGM >> 4) << 24);
+
+__device__ __forceinline__ bool aborted(const GemmSmem& sm) { return *(const volatile int*)&sm.abort != 0; }
+
+__device__ __forceinline__ bool wait_or_abort(unsigned long long* bar, unsigned parity, GemmSmem& sm,
+                                              int* error_word) {
+    if (mbar_wait_bounded(bar, parity)) return true;
+    sm.abort = 1;
+    atomicOr(error_word, 2);
+    return false;
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int& m_blk, int& n_blk) {
+    const int per_group = kGroupM * nt;
+    const int g = tile / per_group;
+    const int r = tile - g * per_group;
+    const int gm = min(kGroupM, mt - g * kGroupM);  // M blocks in this group
+    n_blk = r / gm;
+    m_blk = g * kGroupM + (r - n_blk * gm);
+}
+
+__global__ void __launch_bounds__(kGThreads, 1)
+    classifier_gemm_kernel(const __grid_constant__ CUtensorMap tmap_h, const __grid_constant__ CUtensorMap tmap_w,
+                           GemmLaunch p) {
+    extern __shared__ __align__(16) unsigned char gsm_raw[];
+    GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = (p.batch + kGM - 1) / kGM;
+    const int nt = (p.vocab + kGN - 1) / kGN;
+    const int ntiles = mt * nt;
+    const int ksteps = (p.dim + kGK - 1) / kGK;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&sm.tmem_full[a], 1);
+            mbar_init(&sm.tmem_empty[a], 4);  // one arrival per epilogue warp
+        }
+        mbar_init(&sm.drain, 1);
+        sm.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 2) {
+        tmem_alloc(smem_addr(&sm.tmem_base), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer
+        int stage = 0;
+        unsigned phase = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !aborted(sm); tile += gridDim.x) {
+            int mb, nb;
+            tile_coords(tile, mt, nt, mb, nb);
+            for (int k = 0; k < ksteps; ++k) {
+                if (!wait_or_abort(&sm.empty[stage], phase ^ 1u, sm, p.error_word)) break;
+                mbar_arrive_expect_tx(&sm.full[stage], kStageBytes);
+                tma_load_2d(sm.a[stage], &tmap_h, k * kGK, mb * kGM, &sm.full[stage]);
+                tma_load_2d(sm.b[stage], &tmap_w, k * kGK, nb * kGN, &sm.full[stage]);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        // drain: every stage this thread filled completes before the CTA exits
+        for (int s = 0; s < kStages; ++s) {
+            if (!mbar_wait_bounded(&sm.empty[stage], phase ^ 1u)) break;
+            if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer
+        int stage = 0;
+        unsigned phase = 0;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !aborted(sm); tile += gridDim.x, ++it) {
+            const int acc = it & 1;
+            const unsigned acc_phase = (unsigned)(it >> 1) & 1u;
+            if (!wait_or_abort(&sm.tmem_empty[acc], acc_phase ^ 1u, sm, p.error_word)) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem + (uint32_t)(acc * kGN);
+            bool ok = true;
+            for (int k = 0; k < ksteps; ++k) {
+                if (!wait_or_abort(&sm.full[stage], phase, sm, p.error_word)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = smem_addr(sm.a[stage]), b0 = smem_addr(sm.b[stage]);
+#pragma unroll
+                for (int kk = 0; kk < kGK / 16; ++kk) {
+                    // K advances 16 bf16 = 32 bytes inside the swizzled 128-byte row
+                    tc_mma(d_tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), kIdesc,
+                           (k | kk) != 0 ? 1u : 0u);
+                }
+                tc_commit(&sm.empty[stage]);  // frees the stage when these MMAs are done
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            tc_commit(&sm.tmem_full[acc]);  // accumulator ready
+            if (!ok) break;
+        }
+        // every MMA this thread issued is complete before TMEM is released
+        tc_commit(&sm.drain);
+        mbar_wait_bounded(&sm.drain, 0);
+    } else if (warp >= 4) {
+        // ---- epilogue: warp w reads TMEM lanes 32*(w-4) .. +31
+        const int q = warp - 4;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+            const int acc = it & 1;
+            const unsigned acc_phase = (unsigned)(it >> 1) & 1u;
+            bool got = false;
+            if (lane == 0) got = wait_or_abort(&sm.tmem_full[acc], acc_phase, sm, p.error_word);
+            got = __shfl_sync(kFullMask, got ? 1 : 0, 0) != 0;
+            if (!got || aborted(sm)) break;
+            tc_fence_after();
+            int mb, nb;
+            tile_coords(tile, mt, nt, mb, nb);
+            const int row = mb * kGM + q * 32 + lane;
+            const bool row_ok = row < p.batch;
+            float T = p.temperature;
+            if (p.temperature_rows && row_ok) T = p.temperature_rows[row];
+            const float k2 = __frcp_rn(T) * 1.4426950408889634f;
+            const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kGN);
+#pragma unroll 1
+            for (int c = 0; c < kGN / 32; ++c) {
+                float v[32];
+                tmem_ld32(lane_addr + (uint32_t)(c * 32), v);
+                const int col = nb * kGN + c * 32;
+                if (row_ok && col < p.vocab) {
+                    float4* dst = reinterpret_cast<float4*>(p.logits + (long long)row * p.ld + col);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    if (p.stats) {
+                        // the streaming sampler's pass-1 quantities of this chunk
+                        float mx = v[0], mn = v[0];
+#pragma unroll
+                        for (int j = 1; j < 32; ++j) {
+                            mx = fmaxf(mx, v[j]);
+                            mn = fminf(mn, v[j]);
+                        }
+                        float s2 = 0.0f;
+                        if (T != 0.0f) {
+                            float m2 = -3.4e38f;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) m2 = fmaxf(m2, v[j] * k2);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) s2 += ex2_approx(__fmaf_rn(v[j], k2, -m2));
+                        }
+                        p.stats[(long long)row * p.stats_ld + col / 32] = make_float4(mx, mn, s2, 0.0f);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.tmem_empty[acc]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---- host: tensor maps -------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+// 2-D bf16 K-major tensor [rows, dim] (row stride dim*2 bytes), box [box_rows, 64].
+bool make_tmap(CUtensorMap* m, const void* base, int rows, int dim, int box_rows) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)dim, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)dim * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kGK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t gemm_smem_bytes() { return kGemmSmemBytes; }
+
+int launch_classifier_gemm(const GemmLaunch& p, int num_sms, cudaStream_t stream) {
+    CUtensorMap th, tw;
+    if (!make_tmap(&th, p.h, p.batch, p.dim, kGM) || !make_tmap(&tw, p.w, p.vocab, p.dim, kGN))
+        return -(int)cudaErrorInvalidValue;
+    static std::atomic<unsigned long long> attr_done{0};
+    int dev = 0;
+    cudaError_t e0 = cudaGetDevice(&dev);
+    if (e0 != cudaSuccess) return -(int)e0;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(attr_done.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(classifier_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kGemmSmemBytes);
+        if (e != cudaSuccess) return -(int)e;
+        attr_done.fetch_or(bit);
+    }
+    const int mt = (p.batch + kGM - 1) / kGM, nt = (p.vocab + kGN - 1) / kGN;
+    int grid = num_sms;
+    if (grid > mt * nt) grid = mt * nt;
+    classifier_gemm_kernel<<<grid, kGThreads, kGemmSmemBytes, stream>>>(th, tw, p);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 1 : -(int)e;
+}
+
+}  // namespace b2s

@@ -93,6 +93,14 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// 2^x by the hardware approximation (approximate sums only: binade guesses
+// and nucleus-size estimates, never a value the reference computes).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // xorshift* draw + 24-bit float, llama2.c:1071-1080.
 __device__ __forceinline__ float draw_coin(unsigned long long& s) {
     s ^= s >> 12;
@@ -196,6 +204,50 @@ __device__ __forceinline__ int bin_of(float p) {
 __device__ __forceinline__ float bin_lo(int b) {
     return (b >= kBins - 1) ? 0.0f : __uint_as_float((kOneTop - (uint32_t)b) << kBinShift);
 }
+
+// Sorts the keys of one histogram bin (every key's value shares its top 15
+// bits, so (low 17 value bits, 0x7FFF - index) orders them exactly as the
+// 64-bit key does, for indices < 2^15 - 1, so that every real key is
+// nonzero) with 32-bit keys in registers: half the shuffles of the 64-bit
+// sort.  Not for the last bin, which collects everything below it.
+template <int R>
+__device__ void warp_sort_bin(unsigned long long* seg, int n, int lane) {
+    constexpr int P = 32 * R;
+    uint32_t k[R];
+    uint32_t top = 0u;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int i = r * 32 + lane;
+        const unsigned long long key = (i < n) ? seg[i] : 0ull;
+        const uint32_t vb = (uint32_t)(key >> 32);
+        if (i < n) top = vb >> 17;
+        k[r] = (i < n) ? (((vb & 0x1FFFFu) << 15) | (uint32_t)(0x7FFF - key_index(key))) : 0u;
+    }
+    top = __shfl_sync(kFullMask, top, 0);  // lane 0 always holds a key (n >= 1)
+#pragma unroll
+    for (int size = 2; size <= P; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            uint32_t nk[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int i = r * 32 + lane;
+                const uint32_t other = (stride >= 32) ? k[r ^ (stride >> 5)] : __shfl_xor_sync(kFullMask, k[r], stride);
+                const bool desc = (i & size) == 0;
+                const bool lower = (i & stride) == 0;
+                nk[r] = (lower == desc) ? max(k[r], other) : min(k[r], other);
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) k[r] = nk[r];
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int i = r * 32 + lane;
+        if (i < n) seg[i] = cand_key(__uint_as_float((top << 17) | (k[r] >> 15)), 0x7FFF - (int)(k[r] & 0x7FFFu));
+    }
+}
+
 
 
 }  // namespace

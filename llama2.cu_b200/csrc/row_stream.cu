@@ -58,6 +58,7 @@ constexpr int kKCap = 2048;    // nucleus keys kept on chip (more spill to L2)
 constexpr int kSideCap = 48;   // chunks whose values are kept for replays
 constexpr int kAltCap = 96;    // chunks with an alternative-binade function
 constexpr int kBinsPerThread = kBins / kST;  // 8
+constexpr int kWalkDirect = 512;  // nuclei walked element by element; larger ones by chunk functions
 
 // chunk entry: x=L0 y=L1 z=bits(pbits | flags | alt<<8 | side<<16) w=bits(eb)
 constexpr uint32_t kFClean = 4u, kFValid = 8u, kFAlt = 16u;
@@ -65,7 +66,7 @@ constexpr uint32_t kFClean = 4u, kFValid = 8u, kFAlt = 16u;
 struct StreamSmem {
     unsigned long long kbuf[kKCap];
     int hist[kBins];
-    short bstart[kBins];
+    unsigned short bstart[kBins];  // bin offsets in the nucleus (< 2^16)
     float side[kSideCap][kSC];
     float replay[kSC];
     float4 fn[kChunks];
@@ -83,6 +84,7 @@ struct StreamSmem {
     int dbin;
     int ksel;
     int result;
+    int n0;
     float fval;
 };
 
@@ -165,13 +167,6 @@ __device__ __forceinline__ xm::ChainFn warp_incl_compose(xm::ChainFn f) {
         if (lane >= o) f = xm::chain_compose(y, f);
     }
     return f;
-}
-
-// 2^x by the hardware approximation (only used for binade guesses).
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
 }
 
 __device__ __forceinline__ bool regular_sum(float s) {
@@ -333,6 +328,150 @@ __device__ float resolve_S(StreamSmem& sm, const Ctx& c) {
     return s;
 }
 
+// ---------------------------------------------------------------------------
+// Large nuclei: the serial cumulative sum of the sorted p (llama2.c:1036-1054)
+// walked by chunk functions, as the softmax denominator is resolved.
+// ---------------------------------------------------------------------------
+
+// All threads: chunk t = sorted keys [32t, 32t + 32) of the first n0; its
+// incoming cumulative sum is guessed from a block scan of approximate chunk
+// sums.  Fills fn / alt / wfn (free again once S is resolved).
+__device__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int n0) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nchk = (n0 + kSC - 1) / kSC;
+    if (tid == 0) sm.n_alt = 0;
+    float sig[kStrips], gss[kStrips];
+#pragma unroll
+    for (int sidx = 0; sidx < kStrips; ++sidx) {
+        const int t = sidx * kST + tid;
+        float a = 0.0f;
+        if (t < nchk) {
+            const int cnt = min(kSC, n0 - kSC * t);
+            for (int j = 0; j < cnt; ++j) a += key_prob(kb[kSC * t + j]);
+        }
+        sig[sidx] = a;
+    }
+    float off = 0.0f;
+#pragma unroll
+    for (int sidx = 0; sidx < kStrips; ++sidx) {
+        const ScanF sc = block_scan_f(sig[sidx], sm);
+        gss[sidx] = off + sc.excl;
+        off += sc.total;
+    }
+#pragma unroll 1
+    for (int sidx = 0; sidx < kStrips; ++sidx) {
+        const int t = sidx * kST + tid;
+        const bool valid = t < nchk;
+        const int cnt = valid ? min(kSC, n0 - kSC * t) : 0;
+        uint32_t alt = 0u;
+        const uint32_t eb = valid ? xm::chain_guess_primary(gss[sidx], sig[sidx], alt) : 0u;
+        const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
+        const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
+        float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
+        for (int j = 0; j < cnt; ++j) {
+            const float x = key_prob(kb[kSC * t + j]);
+            v0 = __fadd_rn(v0, x);
+            v1 = __fadd_rn(v1, x);
+            w0 = __fadd_rn(w0, x);
+            w1 = __fadd_rn(w1, x);
+        }
+        const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
+        const bool aclean = valid && alt != 0u && (__float_as_uint(w0) >> 23) == alt && (__float_as_uint(w1) >> 23) == alt;
+        const xm::ChainFn f{__fsub_rn(v0, lo), __fsub_rn(v1, lo1),
+                            (__float_as_uint(v0) & 1u) | ((__float_as_uint(v1) & 1u) << 1)};
+        uint32_t z = (clean ? (f.pbits | kFClean) : 0u) | (valid ? kFValid : 0u);
+        if (aclean) {
+            const int ai = atomicAdd(&sm.n_alt, 1);
+            if (ai < kAltCap) {
+                sm.alt[ai] = make_float4(__fsub_rn(w0, alo), __fsub_rn(w1, alo1),
+                                         __uint_as_float((__float_as_uint(w0) & 1u) |
+                                                         ((__float_as_uint(w1) & 1u) << 1) | kFClean),
+                                         __uint_as_float(alt));
+                z |= kFAlt | ((uint32_t)ai << 8);
+            }
+        }
+        if (valid) sm.fn[t] = make_float4(f.L0, f.L1, __uint_as_float(z), __uint_as_float(eb));
+        const uint32_t eb0 = __shfl_sync(kFullMask, eb, 0);
+        const bool uni = __all_sync(kFullMask, !valid || (clean && eb == eb0 && !(z & kFAlt)));
+        const xm::ChainFn F = warp_incl_compose((valid && clean) ? f : xm::chain_identity());
+        if (lane == 31)
+            sm.wfn[sidx * kSW + warp] =
+                make_float4(F.L0, F.L1, __uint_as_float(F.pbits | (uni ? kFClean : 0u)), __uint_as_float(eb0));
+    }
+    __syncthreads();
+}
+
+// Warp 0: the first i < n with cum_i = fl(cum_{i-1} + p_i) > theta (cum is
+// then cum_i), or n (cum = cum_{n-1}), over the chunk functions of
+// build_walk_fns (built for n0 >= n keys).  Whole segments and chunks are
+// applied while they stay in one binade and end at or below theta; the chunk
+// that crosses theta or a binade is walked element by element.
+__device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, int n, float theta, float& cum) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.0f;
+    const int nchk = (n + kSC - 1) / kSC;
+    const int nseg = (nchk + 31) / 32;
+    for (int seg = 0; seg < nseg; ++seg) {
+        const int cnt = min(32, nchk - seg * 32);
+        const float4 wf = sm.wfn[seg];
+        const uint32_t wz = __float_as_uint(wf.z);
+        // a whole segment only when all of its chunks are inside [0, n)
+        if ((wz & kFClean) && seg * 32 * kSC + 32 * kSC <= n) {
+            float s2 = s;
+            if (xm::chain_apply(s2, __float_as_uint(wf.w), xm::ChainFn{wf.x, wf.y, wz & 3u}) && !(s2 > theta)) {
+                s = s2;
+                continue;
+            }
+        }
+        // chunks wholly inside [0, n) may use their functions
+        const int t_lane = seg * 32 + lane;
+        const bool whole = (t_lane + 1) * kSC <= n;
+        const float4 ent = (lane < cnt) ? sm.fn[t_lane] : make_float4(0, 0, 0, 0);
+        const uint32_t ez = __float_as_uint(ent.z);
+        float4 aent = make_float4(0, 0, 0, 0);
+        if (lane < cnt && (ez & kFAlt)) aent = sm.alt[(ez >> 8) & 0xFFu];
+        const uint32_t az = __float_as_uint(aent.z);
+        int cpos = 0;
+        while (cpos < cnt) {
+            if (regular_sum(s)) {
+                const uint32_t eb = xm::binade_of(s);
+                const bool use_p = whole && (ez & kFClean) && __float_as_uint(ent.w) == eb;
+                const bool use_a = whole && !use_p && (ez & kFAlt) && (az & kFClean) && __float_as_uint(aent.w) == eb;
+                const bool has = (lane >= cpos) && (lane < cnt) && (use_p || use_a);
+                xm::ChainFn f = xm::chain_identity();
+                if (has) f = use_p ? xm::ChainFn{ent.x, ent.y, ez & 3u} : xm::ChainFn{aent.x, aent.y, az & 3u};
+                const unsigned hm = __ballot_sync(kFullMask, has || lane < cpos);
+                const int fi = (~hm) ? (__ffs(~hm) - 1) : 32;
+                f = warp_incl_compose(f);
+                const float hi = __uint_as_float((eb + 1u) << 23);
+                const float L = (__float_as_uint(s) & 1u) ? f.L1 : f.L0;
+                const bool fits_b = (lane < fi) && (L <= __fsub_rn(hi, s));
+                const float sl = __fadd_rn(s, L);
+                // chunks [cpos, m) end inside the binade and at or below theta
+                const bool inb = (lane < cpos) || (fits_b && !(sl > theta));
+                const unsigned inm = __ballot_sync(kFullMask, inb);
+                const int m = (~inm) ? (__ffs(~inm) - 1) : 32;
+                if (m > cpos) {
+                    s = __shfl_sync(kFullMask, sl, m - 1);
+                    cpos = m;
+                }
+            }
+            if (cpos < cnt) {
+                const int base = (seg * 32 + cpos) * kSC;
+                const int ne = min(kSC, n - base);
+                const int k = warp_chain([&](int i) { return key_prob(kb[base + i]); }, ne, s, theta);
+                if (k < ne) {
+                    cum = s;
+                    return base + k;
+                }
+                ++cpos;
+            }
+        }
+    }
+    cum = s;
+    return n;
+}
+
 __device__ void defer_row_s(const RowLaunch& p, int row) {
     const int k = atomicAdd(p.defer_count, 1);
     p.defer_rows[k] = row;
@@ -477,11 +616,21 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
         const float k2 = c.rT * 1.4426950408889634f;  // log2(e)/T, approximate scale
         float mxl = -INFINITY, mnl = INFINITY, M2loc = -3.4e38f;
         float cm2[kStrips], cs2[kStrips];
+        const float4* stats = p.stats ? p.stats + (long long)row * p.stats_ld : nullptr;
 #pragma unroll
         for (int sidx = 0; sidx < kStrips; ++sidx) {
             const int t = sidx * kST + tid;
             float m2 = -3.4e38f, s2 = 0.0f;
-            if (t < nch) {
+            if (stats) {
+                // the same quantities from the classifier GEMM epilogue
+                if (t < nch) {
+                    const float4 q = stats[t];
+                    mxl = fmaxf(mxl, q.x);
+                    mnl = fminf(mnl, q.y);
+                    m2 = fmaxf(m2, (k2 > 0.0f ? q.x : q.y) * k2);
+                    s2 = q.z;
+                }
+            } else if (t < nch) {
                 float a[kSC];
                 load_chunk(c, t, a);  // eight loads in flight
                 const int cnt = min(kSC, V - t * kSC);
@@ -691,7 +840,8 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
             }
             // the nucleus lives on chip, or in the CTA's L2 scratch
             unsigned long long* kb = (K <= kKCap) ? sm.kbuf : super;
-            const bool fits = K <= 4096;
+            // the L2 scratch holds any nucleus (ws_stride >= V + 4096 keys)
+            const bool fits = K <= p.ws_stride;
             if (fits) {
                 // bin offsets (hist becomes the scatter cursor)
                 int run = cex;
@@ -699,7 +849,7 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                 for (int q = 0; q < kBinsPerThread; ++q) {
                     const int b = tid * kBinsPerThread + q;
                     if (b <= D) {
-                        sm.bstart[b] = (short)run;
+                        sm.bstart[b] = (unsigned short)run;
                         sm.hist[b] = run;
                         run += h[q];
                     }
@@ -781,10 +931,17 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                         const int ss = __shfl_sync(kFullMask, s0, src);
                         const int nn = __shfl_sync(kFullMask, n, src);
                         unsigned long long* seg = kb + ss;
-                        if (nn <= 32) warp_sort_desc<1>(seg, nn, lane);
-                        else if (nn <= 64) warp_sort_desc<2>(seg, nn, lane);
-                        else if (nn <= 128) warp_sort_desc<4>(seg, nn, lane);
-                        else warp_sort_desc<8>(seg, nn, lane);
+                        if (b0 + src < kBins - 1 && V < 0x7FFF) {
+                            if (nn <= 32) warp_sort_bin<1>(seg, nn, lane);
+                            else if (nn <= 64) warp_sort_bin<2>(seg, nn, lane);
+                            else if (nn <= 128) warp_sort_bin<4>(seg, nn, lane);
+                            else warp_sort_bin<8>(seg, nn, lane);
+                        } else {
+                            if (nn <= 32) warp_sort_desc<1>(seg, nn, lane);
+                            else if (nn <= 64) warp_sort_desc<2>(seg, nn, lane);
+                            else if (nn <= 128) warp_sort_desc<4>(seg, nn, lane);
+                            else warp_sort_desc<8>(seg, nn, lane);
+                        }
                     }
                 }
             }
@@ -793,37 +950,69 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
             if (!fits || sm.flag) {
                 defer = true;
             } else {
-                // p = fl(e/S) in place of e; flag equal-p runs out of index order
-                bool bad = false;
-                for (int i = tid; i < K; i += kST) {
-                    const unsigned long long k = kb[i];
-                    const float pv = __fdiv_rn(key_prob(k), S);
-                    kb[i] = ((unsigned long long)__float_as_uint(pv) << 32) | (k & 0xFFFFFFFFull);
-                }
+                // p = fl(e/S) in place of e (Markstein division: correctly
+                // rounded for S in [1, 2^15] and e >= 2^-60).  The same pass
+                // finds the end of the candidates proper (p >= cutoff form a
+                // prefix) from each key's successor, and whether any equal-p
+                // run exists.  Four keys per thread in flight.
+                const float rS = __frcp_rn(S);
+                auto to_p = [&](float e) {
+                    const float q = __fmul_rn(e, rS);
+                    return __fmaf_rn(__fmaf_rn(-q, S, e), rS, q);
+                };
+                if (tid == 0) sm.n0 = 0;
                 __syncthreads();
-                for (int i = tid; i + 1 < K; i += kST) {
-                    const unsigned long long a = kb[i], b = kb[i + 1];
-                    bad |= ((a >> 32) == (b >> 32)) && (key_index(a) > key_index(b));
+                bool any_run = false;
+                for (int base = 0; base < K; base += 4 * kST) {  // uniform trip count (barrier inside)
+                    const int i0 = base + tid;
+                    unsigned long long k[4], kn[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int i = i0 + u * kST;
+                        k[u] = (i < K) ? kb[i] : 0ull;
+                        kn[u] = (i + 1 < K) ? kb[i + 1] : 0ull;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int i = i0 + u * kST;
+                        if (i < K) {
+                            const float pv = to_p(key_prob(k[u]));
+                            const bool has_next = i + 1 < K;
+                            const float pn = has_next ? to_p(key_prob(kn[u])) : -1.0f;
+                            any_run |= (pn == pv);
+                            if (pv >= cutoff && !(pn >= cutoff)) sm.n0 = i + 1;
+                            k[u] = ((unsigned long long)__float_as_uint(pv) << 32) | (k[u] & 0xFFFFFFFFull);
+                        }
+                    }
+                    __syncthreads();  // every key of this round read before any is rewritten
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (i0 + u * kST < K) kb[i0 + u * kST] = k[u];
                 }
-                if (__syncthreads_or(bad) && tid == 0) {
-                    for (bool swapped = true; swapped;) {
-                        swapped = false;
-                        for (int i = 0; i + 1 < K; ++i) {
-                            const unsigned long long a = kb[i], b = kb[i + 1];
-                            if ((a >> 32) == (b >> 32) && key_index(a) > key_index(b)) {
-                                kb[i] = b;
-                                kb[i + 1] = a;
-                                swapped = true;
+                // equal-p runs (sorted by e, so contiguous) go to index order,
+                // glibc qsort's order for ties (rare: runs are a few keys)
+                if (__syncthreads_or(any_run)) {
+                    for (int i = tid; i + 1 < K; i += kST) {
+                        const unsigned long long a = kb[i];
+                        if ((a >> 32) == (kb[i + 1] >> 32) && (i == 0 || (kb[i - 1] >> 32) != (a >> 32))) {
+                            int j = i + 1;
+                            while (j < K && (kb[j] >> 32) == (a >> 32)) ++j;
+                            for (int x = i + 1; x < j; ++x) {  // insertion sort by index
+                                const unsigned long long kx = kb[x];
+                                int y = x - 1;
+                                while (y >= i && key_index(kb[y]) > key_index(kx)) {
+                                    kb[y + 1] = kb[y];
+                                    --y;
+                                }
+                                kb[y + 1] = kx;
                             }
                         }
                     }
+                    __syncthreads();
                 }
-                __syncthreads();
-                // candidates proper (p >= cutoff) form a prefix
-                int n0loc = 0;
-                for (int i = tid; i < K; i += kST) n0loc += (key_prob(kb[i]) >= cutoff) ? 1 : 0;
-                int n0;
-                block_scan_i(n0loc, sm, n0);
+                const int n0 = sm.n0;
+                const bool big = n0 > kWalkDirect;
+                if (big) build_walk_fns(sm, kb, n0);  // all threads
                 if (warp == 0) {
                     int res = -1;
                     if (n0 == 0) {
@@ -831,12 +1020,13 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                     } else {
                         auto get = [&](int i) { return key_prob(kb[i]); };
                         float cum = 0.0f;
-                        int last = warp_chain(get, n0, cum, topp);  // llama2.c:1036-1043
+                        // llama2.c:1036-1043
+                        int last = big ? walk_chunks(sm, kb, n0, topp, cum) : warp_chain(get, n0, cum, topp);
                         if (last >= n0) last = all_cand ? n0 - 1 : -1;  // llama2.c:1037
                         if (last >= 0) {
                             const float r = __fmul_rn(coin, cum);  // llama2.c:1046
                             float s3 = 0.0f;
-                            int k = warp_chain(get, last + 1, s3, r);
+                            int k = big ? walk_chunks(sm, kb, last + 1, r, s3) : warp_chain(get, last + 1, s3, r);
                             if (k > last) k = last;  // llama2.c:1055
                             res = key_index(kb[k]);
                         }

@@ -71,6 +71,11 @@ struct DeviceCtx {
     unsigned long long* d_state = nullptr;
     int* d_ids = nullptr;
     int rows_cap = 0;
+    // fused classifier: logits and per-chunk statistics
+    float* d_flogits = nullptr;
+    size_t flogits_cap = 0;
+    float4* d_stats = nullptr;
+    size_t stats_cap = 0;
 };
 
 std::mutex g_mu;
@@ -150,7 +155,8 @@ bool stream_layout_ok(const float* logits, int V, long long ld) {
 int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
              const float* temperature_rows, const float* topp_rows, const float* coins,
              unsigned long long* rng_state, int* out_ids, float* probs_out, int* row_flags,
-             void* workspace, size_t workspace_bytes, cudaStream_t stream, int force_mode) {
+             void* workspace, size_t workspace_bytes, cudaStream_t stream, int force_mode,
+             const float4* stats = nullptr, long long stats_ld = 0) {
     g_last_launches = 0;
     if (!cfg || !logits || !out_ids) return fail(SAMPLER_E_INVALID, "null config, logits or out_ids");
     const int V = cfg->vocab_size;
@@ -227,6 +233,8 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
         b2s::RowLaunch q = p;
         q.workspace = stream_ws;
         q.ws_stride = (long long)stream_stride(V);
+        q.stats = stats;
+        q.stats_ld = stats_ld;
         const int n = b2s::launch_row_stream(q, stream_ctas(c, batch), stream);
         if (n < 0) return fail(SAMPLER_E_CUDA, "stream launch: %s", cudaGetErrorString((cudaError_t)(-n)));
         launches += n + 1;
@@ -400,6 +408,72 @@ int sampler_batched(const SamplerBatchConfig* cfg, const float* logits, int batc
                     void* workspace, size_t workspace_bytes, void* stream) {
     return dispatch(cfg, logits, batch, ld, temperature_rows, topp_rows, coins, rng_state, out_ids, probs_out,
                     row_flags, workspace, workspace_bytes, (cudaStream_t)stream, 0);
+}
+
+// Fused variant: classifier GEMM (tcgen05) with the statistics epilogue,
+// then the streaming sampler fed by those statistics.
+int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, const void* wcls, int batch, int dim,
+                            const float* temperature_rows, const float* topp_rows, const float* coins,
+                            unsigned long long* rng_state, int* out_ids, float* logits_out, int* row_flags,
+                            void* stream) {
+    g_last_launches = 0;
+    if (!cfg || !hidden || !wcls || !out_ids) return fail(SAMPLER_E_INVALID, "null config, hidden, wcls or out_ids");
+    const int V = cfg->vocab_size;
+    if (batch < 0 || dim < 8 || (dim % 8) != 0 || V < 32 || (V % 32) != 0)
+        return fail(SAMPLER_E_INVALID, "bad sizes: batch=%d dim=%d (multiple of 8) vocab=%d (multiple of 32)", batch,
+                    dim, V);
+    if (V > SAMPLER_MAX_VOCAB)
+        return fail(SAMPLER_E_UNSUPPORTED, "vocab_size %d above SAMPLER_MAX_VOCAB %d", V, SAMPLER_MAX_VOCAB);
+    if (cfg->flags & SAMPLER_FLAG_PROBS_IN) return fail(SAMPLER_E_INVALID, "PROBS_IN does not apply to the fused call");
+    if (((uintptr_t)hidden & 15u) || ((uintptr_t)wcls & 15u) || ((uintptr_t)logits_out & 15u))
+        return fail(SAMPLER_E_INVALID, "hidden, wcls and logits_out must be 16-byte aligned");
+    if (batch == 0) return SAMPLER_OK;
+    DeviceCtx* c = nullptr;
+    int rc = get_ctx(&c);
+    if (rc) return rc;
+    const size_t nlog = (size_t)batch * (size_t)V;
+    const long long sld = V / 32;
+    const size_t nst = (size_t)batch * (size_t)sld;
+    float* logits = logits_out;
+    float4* stats = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!logits && c->flogits_cap < nlog) {
+            if (c->d_flogits) cudaFree(c->d_flogits);
+            c->d_flogits = nullptr;
+            c->flogits_cap = 0;
+            B2S_CUDA(cudaMalloc(&c->d_flogits, nlog * sizeof(float)));
+            c->flogits_cap = nlog;
+        }
+        if (c->stats_cap < nst) {
+            if (c->d_stats) cudaFree(c->d_stats);
+            c->d_stats = nullptr;
+            c->stats_cap = 0;
+            B2S_CUDA(cudaMalloc(&c->d_stats, nst * sizeof(float4)));
+            c->stats_cap = nst;
+        }
+        if (!logits) logits = c->d_flogits;
+        stats = c->d_stats;
+    }
+    b2s::GemmLaunch g{};
+    g.h = hidden;
+    g.w = wcls;
+    g.batch = batch;
+    g.dim = dim;
+    g.vocab = V;
+    g.logits = logits;
+    g.ld = V;
+    g.stats = stats;
+    g.stats_ld = sld;
+    g.temperature = cfg->temperature;
+    g.temperature_rows = temperature_rows;
+    g.error_word = c->error_word;
+    const int n = b2s::launch_classifier_gemm(g, c->num_sms, (cudaStream_t)stream);
+    if (n < 0) return fail(SAMPLER_E_CUDA, "classifier GEMM launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+    rc = dispatch(cfg, logits, batch, V, temperature_rows, topp_rows, coins, rng_state, out_ids, nullptr, row_flags,
+                  nullptr, 0, (cudaStream_t)stream, 0, stats, sld);
+    g_last_launches += n;
+    return rc;
 }
 
 int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,

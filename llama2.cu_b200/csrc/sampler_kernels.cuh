@@ -36,6 +36,28 @@ struct RowLaunch {
     int* defer_rows;
     const int* row_list;
     const int* row_count;
+    // optional per-chunk statistics of the rows (max l, min l, approximate
+    // sum of exp2(l*k2 - max(l*k2)), unused), written by the classifier GEMM
+    // epilogue: the streaming kernel then skips its first pass
+    const float4* stats;
+    long long stats_ld;  // float4 entries per row
+};
+
+// The classifier GEMM of the fused variant: logits[B, V] = H[B, D] . W[V, D]^T
+// (bf16 in, fp32 out) plus the per-chunk statistics of each row.
+struct GemmLaunch {
+    const void* h;   // bf16 [batch, dim], row-major
+    const void* w;   // bf16 [vocab, dim], row-major
+    int batch;
+    int dim;
+    int vocab;       // multiple of 32
+    float* logits;   // fp32 [batch, ld]
+    long long ld;    // multiple of 4
+    float4* stats;   // [batch, stats_ld] or nullptr
+    long long stats_ld;
+    float temperature;
+    const float* temperature_rows;
+    int* error_word;
 };
 
 struct ArgmaxLaunch {
@@ -59,5 +81,8 @@ int stream_ctas_per_sm();
 // the rest go to the deferred list).  workspace: ws_stride >= vocab u64
 // entries per CTA.
 int launch_row_stream(const RowLaunch& p, int num_ctas, cudaStream_t stream);
+// Persistent tcgen05 GEMM, one CTA per SM (at most num_sms CTAs).
+int launch_classifier_gemm(const GemmLaunch& p, int num_sms, cudaStream_t stream);
+size_t gemm_smem_bytes();
 
 }  // namespace b2s

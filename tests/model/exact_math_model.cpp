@@ -134,9 +134,45 @@ static bool check_row(const std::vector<float>& a, float s_init) {
     return s == tot;
 }
 
+// Markstein division q = RN(x*r), q' = RN(q + RN(x - q*d)*r) with r = RN(1/d)
+// (P. Markstein, IBM J. Res. Dev. 34(1), 1990) against IEEE division, on the
+// two ranges the kernels use it for: x = l/T with |T| in [2^-10, 2^10] and
+// |l| in [2^-60, 2^60], and p = e/S with S in [1, 2^15] and e in [2^-60, 1].
+static float markstein(float x, float d, float r) {
+    const float q = x * r;
+    return fmaf(fmaf(-q, d, x), r, q);
+}
+
+static int check_div(long stride) {
+    std::mt19937_64 rng(777);
+    std::uniform_real_distribution<double> U(0, 1);
+    long long n = 0, bad = 0;
+    for (int range = 0; range < 2; ++range) {
+        std::vector<float> ds = range == 0 ? std::vector<float>{0.7f, 0.8f, 1.0f, 0x1p-10f, 0x1.fffffep9f, -0.5f}
+                                           : std::vector<float>{1.0f, 1.5f, 32000.0f, 0x1.fffffep14f, 12345.678f};
+        while (ds.size() < 64) {
+            const double m = 1.0 + U(rng);
+            ds.push_back(range == 0 ? (float)ldexp(m, (int)(U(rng) * 20) - 10) : (float)ldexp(m, (int)(U(rng) * 15)));
+        }
+        const uint32_t lo = xm_f2u_host(0x1p-60f), hi = xm_f2u_host(range == 0 ? 0x1p60f : 1.0f);
+        for (float d : ds) {
+            const float r = 1.0f / d;
+            for (uint64_t b = lo; b <= hi; b += (uint64_t)stride * 101) {
+                for (int sg = 0; sg < (range == 0 ? 2 : 1); ++sg) {
+                    const float x = xm_u2f_host((uint32_t)b | (sg ? 0x80000000u : 0u));
+                    ++n;
+                    if (xm_f2u_host(markstein(x, d, r)) != xm_f2u_host(x / d)) ++bad;
+                }
+            }
+        }
+    }
+    printf("division: %lld quotients, %lld differ from IEEE division\n", n, bad);
+    return bad != 0;
+}
+
 int main(int argc, char** argv) {
     const long stride = argc > 1 ? atol(argv[1]) : 97;
-    int rc = check_exp(stride);
+    int rc = check_exp(stride) | check_div(stride);
     std::mt19937_64 rng(12345);
     std::normal_distribution<double> N(0, 1);
     std::uniform_real_distribution<double> U(0, 1);

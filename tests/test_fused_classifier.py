@@ -1,0 +1,114 @@
+"""GPU parity of the fused variant: the tcgen05 classifier GEMM (logits =
+hidden . wcls^T, bf16 in, fp32 accumulate) and the sampling of its rows.
+
+Bars:
+  * logits against a plain PyTorch fp32 matmul of the same bf16 operands
+    (exact products, only the summation order differs): |diff| <= LOGIT_ATOL
+    plus LOGIT_RTOL times the sum of |products| of the entry;
+  * ids, states and flags: identical to sampler_batched() run on the fused
+    call's own logits (the epilogue statistics only replace the sampler's
+    first pass), and those ids pass the end-to-end rule against the oracle.
+"""
+import numpy as np
+import pytest
+import torch
+
+from test_gpu_parity import check_e2e
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0")
+LOGIT_ATOL = 1e-5
+LOGIT_RTOL = 2e-6
+
+
+def operands(B, D, V, seed):
+    g = torch.Generator().manual_seed(seed)
+    h = torch.randn(B, D, generator=g).to(torch.bfloat16)
+    w = (torch.randn(V, D, generator=g) * 0.02).to(torch.bfloat16)
+    return h.to(DEV), w.to(DEV)
+
+
+def fused(pkg, h, w, temp, topp, seeds, topp_rows=None, temp_rows=None):
+    B, V = h.shape[0], w.shape[0]
+    st = torch.from_numpy(np.asarray(seeds, np.uint64).view(np.int64).copy()).to(DEV)
+    logits = torch.empty(B, V, device=DEV)
+    flags = torch.full((B,), -1, dtype=torch.int32, device=DEV)
+    tr = None if topp_rows is None else torch.from_numpy(np.asarray(topp_rows, np.float32)).to(DEV)
+    te = None if temp_rows is None else torch.from_numpy(np.asarray(temp_rows, np.float32)).to(DEV)
+    ids = pkg.classifier_sample_fused(h, w, temp, topp, st, topp_rows=tr, temperature_rows=te, logits_out=logits,
+                                      row_flags=flags)
+    torch.cuda.synchronize()
+    return dict(ids=ids.cpu().numpy(), states=st.cpu().numpy().view(np.uint64), logits=logits,
+                flags=flags.cpu().numpy())
+
+
+def unfused(pkg, logits, temp, topp, seeds, topp_rows=None, temp_rows=None):
+    B = logits.shape[0]
+    st = torch.from_numpy(np.asarray(seeds, np.uint64).view(np.int64).copy()).to(DEV)
+    flags = torch.full((B,), -1, dtype=torch.int32, device=DEV)
+    tr = None if topp_rows is None else torch.from_numpy(np.asarray(topp_rows, np.float32)).to(DEV)
+    te = None if temp_rows is None else torch.from_numpy(np.asarray(temp_rows, np.float32)).to(DEV)
+    ids = pkg.sample_batched(logits, temp, topp, st, topp_rows=tr, temperature_rows=te, row_flags=flags)
+    torch.cuda.synchronize()
+    return dict(ids=ids.cpu().numpy(), states=st.cpu().numpy().view(np.uint64), flags=flags.cpu().numpy())
+
+
+def check_logits(h, w, logits):
+    ref = h.float() @ w.float().t()
+    bound = h.float().abs() @ w.float().abs().t()
+    err = (logits - ref).abs()
+    ok = err <= LOGIT_ATOL + LOGIT_RTOL * bound
+    assert bool(ok.all()), f"max |diff| {err.max().item():.3g}, worst ratio {(err / (bound + 1e-30)).max().item():.3g}"
+
+
+# (B, D, V): the decode shape with fewer rows, then tails in every dimension
+# (rows % 128, dim % 64, vocab % 256)
+SHAPES = [(256, 4096, 32000), (300, 4096, 4064), (130, 520, 32000), (1, 64, 256)]
+
+
+@pytest.mark.parametrize("B,D,V", SHAPES)
+def test_fused_logits_and_ids(pkg, orc, B, D, V):
+    h, w = operands(B, D, V, seed=4 + B)
+    seeds = pkg.workloads.row_seeds(B)
+    topps = np.where(np.arange(B) % 2 == 0, 0.9, 0.95).astype(np.float32)
+    out = fused(pkg, h, w, 0.8, 0.9, seeds, topp_rows=topps)
+    check_logits(h, w, out["logits"])
+    ref = unfused(pkg, out["logits"], 0.8, 0.9, seeds, topp_rows=topps)
+    assert np.array_equal(out["ids"], ref["ids"])
+    assert np.array_equal(out["states"], ref["states"])
+    assert np.array_equal(out["flags"], ref["flags"])
+    n = min(B, 64)
+    x = out["logits"][:n].cpu().numpy()
+    ref_ids, ref_st, ref_p = orc.sample_batch(x, 0.8, 0.9, seeds[:n], topp_rows=topps[:n], probs_out=True)
+    assert np.array_equal(out["states"][:n], ref_st)
+    check_e2e(orc, out["ids"][:n], ref_ids, ref_p, seeds[:n], topps[:n])
+
+
+def test_fused_greedy_and_mixed_rows(pkg, orc):
+    B, D, V = 200, 1024, 32000
+    h, w = operands(B, D, V, seed=99)
+    temps = np.where(np.arange(B) % 4 == 0, 0.0, 0.7).astype(np.float32)
+    topps = np.where(np.arange(B) % 3 == 0, 1.0, 0.9).astype(np.float32)
+    seeds = pkg.workloads.row_seeds(B, seed=7)
+    out = fused(pkg, h, w, 0.7, 0.9, seeds, topp_rows=topps, temp_rows=temps)
+    check_logits(h, w, out["logits"])
+    ref = unfused(pkg, out["logits"], 0.7, 0.9, seeds, topp_rows=topps, temp_rows=temps)
+    assert np.array_equal(out["ids"], ref["ids"]) and np.array_equal(out["states"], ref["states"])
+    x = out["logits"].cpu().numpy()
+    greedy = np.nonzero(temps == 0.0)[0]
+    assert [int(out["ids"][r]) for r in greedy] == [orc.argmax(x[r]) for r in greedy]
+
+
+def test_fused_all_greedy(pkg, orc):
+    B, D, V = 64, 4096, 32000
+    h, w = operands(B, D, V, seed=5)
+    out = fused(pkg, h, w, 0.0, 0.9, pkg.workloads.row_seeds(B))
+    x = out["logits"].cpu().numpy()
+    assert out["ids"].tolist() == [orc.argmax(r) for r in x]
+
+
+def test_fused_rejects_bad_shapes(pkg):
+    h, w = operands(4, 64, 100, seed=1)  # vocab not a multiple of 32
+    with pytest.raises(pkg.SamplerError):
+        pkg.classifier_sample_fused(h, w, 1.0, 0.9, torch.zeros(4, dtype=torch.int64, device=DEV))

@@ -204,6 +204,19 @@ def test_large_nucleus_deferred_from_pipeline(pkg, orc):
     check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, np.full(8, 0.95))
 
 
+@pytest.mark.parametrize("sigma,temp,topp", [(1.6, 0.8, 0.9), (1.0, 1.0, 0.99), (2.5, 0.7, 0.5), (1.2, 0.9, 0.95)])
+def test_large_nucleus_fast_path(pkg, orc, sigma, temp, topp):
+    """Nuclei of hundreds to thousands of tokens stay in the streaming kernel
+    (the cumulative walk by chunk functions) and match the oracle."""
+    x = np.random.default_rng(23).normal(0, sigma, (64, 32000)).astype(np.float32)
+    seeds = np.arange(64, dtype=np.uint64) + 500
+    out = gpu_sample(pkg, x, temp, topp, seeds=seeds)
+    assert not (out["flags"] & pkg.ROW_SLOW_PATH).any()
+    ref_ids, ref_st, ref_p = orc.sample_batch(x, temp, topp, seeds, probs_out=True)
+    assert np.array_equal(out["states"], ref_st)
+    check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, np.full(64, topp))
+
+
 def test_topp_without_probability_writeback_same_ids(pkg):
     """The fast path (no probs_out) computes p only for candidates; ids must
     not change."""
