@@ -1,6 +1,7 @@
 """Benchmark: batched top-p sampling of B x 32000 fp32 logits on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload topp|fused]
 
 One step = one pass of the logits -> token path over one batch: the top-p
 workload (per GPU B=4096 rows x V=32000, Gumbel + Zipf-bonus logits,
@@ -14,6 +15,12 @@ same metric through the host-buffer C-ABI entry point (sampler_batched_host)
 with the H2D copy of the logits from pinned memory and the D2H copy of the
 ids inside the timed region.  `--impl reference` times the reference's own
 CPU sampler (llama2.c sample() over rows, OpenMP over the host cores).
+
+`--workload fused` measures the fused variant instead: the classifier
+projection of B = 8192 bf16 hidden states (dim 4096, sharded over the GPUs)
+against a bf16 wcls [32000, 4096] on the tensor cores, then top-p sampling
+(T = 0.8, topp 0.9) of the resulting rows; its roofline is the GEMM kernel
+against the measured bf16 tensor peak.
 """
 import argparse
 import json
@@ -41,6 +48,18 @@ def load_json(path, default=None):
             return json.load(f)
     except Exception:
         return default
+
+
+def profiled_traffic(name):
+    """DRAM bytes per launch (read + write) recorded by an ncu summary under
+    profiles/ (the `traffic_bytes_per_launch:` line), or None."""
+    import re
+    try:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
+            m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", f.read(), re.M)
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
 
 
 def dist_env():
@@ -114,8 +133,10 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_baseline(x, topp_rows, rows, use_ref=True):
-    """The reference's own sampler over `rows` rows on all host threads."""
+def cpu_baseline(x, topp_rows, rows, use_ref=True, min_seconds=10.0):
+    """The reference's own sampler on all host threads: passes over the first
+    `rows` rows of the workload, repeated until at least `min_seconds` of CPU
+    work (a bounded sample of the same workload)."""
     import oracle
     if use_ref and oracle.ref_available():
         lib, kind = oracle.ref_sampler(), "reference"
@@ -126,10 +147,16 @@ def cpu_baseline(x, topp_rows, rows, use_ref=True):
     from __graft_entry__ import load_package
     seeds = load_package().workloads.row_seeds(rows)
     t0 = time.perf_counter()
-    lib.sample_batch(x[:rows], TEMP, 0.9, seeds, topp_rows=topp_rows[:rows], nthreads=threads)
-    dt = time.perf_counter() - t0
-    return dict(value=rows / dt, unit="tokens/s", cores=threads, kind=kind,
-                sample=f"{rows} rows of the top-p workload (llama2.c sample() per row, OpenMP over rows), {dt:.2f} s")
+    passes = 0
+    while True:
+        lib.sample_batch(x[:rows], TEMP, 0.9, seeds, topp_rows=topp_rows[:rows], nthreads=threads)
+        passes += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    return dict(value=passes * rows / dt, unit="tokens/s", cores=threads, kind=kind,
+                sample=f"{passes} passes over {rows} rows of the top-p workload (llama2.c sample() per row, "
+                       f"OpenMP over rows), {dt:.1f} s")
 
 
 def run_reference(args):
@@ -162,6 +189,110 @@ def run_reference(args):
                                   sample=f"{rows} rows per step, llama2.c sample() per row, OpenMP over rows"),
                 e2e=dict(value=value, unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_fused(args):
+    """Fused classifier + sampling, global batch 8192 sharded by rows."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    pkg = load_package()
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    f = pkg.workloads.fused()
+    Bg, D = f["hidden"].shape
+    V = f["wcls"].shape[0]
+    row0 = rank * Bg // world
+    B = (rank + 1) * Bg // world - row0
+    h_host = torch.from_numpy(f["hidden"][row0:row0 + B].view(np.int16)).view(torch.bfloat16)
+    h = h_host.to(dev)
+    w = torch.from_numpy(f["wcls"].view(np.int16)).view(torch.bfloat16).to(dev)
+    states = torch.empty(B, dtype=torch.int64, device=dev)
+    ids = torch.empty(B, dtype=torch.int32, device=dev)
+    logits = torch.empty(B, V, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    T, TOPP = f["temperature"], f["topp"]
+
+    def step():
+        pkg.seed_states(states, f["seed"], row0)
+        pkg.classifier_sample_fused(h, w, T, TOPP, states, out_ids=ids, stream=stream)
+        return pkg.last_launch_count() + 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    time.sleep(0.25)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    ev0.record(stream)
+    for _ in range(args.steps):
+        launches += step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    # the GEMM kernel alone, per launch
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in kev:
+        a.record(stream)
+        pkg.classifier_logits(h, w, logits_out=logits, stream=stream)
+        b.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    gemm_ms = float(np.mean([a.elapsed_time(b) for a, b in kev]))
+    # end to end: hidden states from pinned host memory, ids back to the host
+    pin = h_host.pin_memory()
+    ids_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        h.copy_(pin, non_blocking=True)
+        step()
+        ids_host.copy_(ids, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    t = torch.tensor([ms, gemm_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, gemm_ms, e2e_ms = (float(v) for v in t)
+    if rank == 0:
+        peaks = load_json(os.path.join(ROOT, "MEASURED_PEAKS.json"), {})
+        peak, note = peaks.get("bf16_tflops"), "of measured (burst)"
+        if not peak:
+            peak, note = 1590.0, "of fallback"
+        flops = 2.0 * B * D * V
+        achieved = flops / (gemm_ms * 1e-3) / 1e12
+        line = dict(metric="fused classifier (bf16 tcgen05 GEMM) + top-p sampling, sampled tokens/sec",
+                    value=Bg / (ms * 1e-3), unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
+                    ms_per_step=ms, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="bf16",
+                    data="synthetic (seeded numpy PCG64: H ~ N(0,1), wcls ~ N(0, 0.02^2), bf16)",
+                    config=dict(workload=f"fused: H bf16 [{Bg},{D}] x wcls bf16 [{V},{D}] -> fp32 logits, "
+                                         f"T={T}, topp {TOPP}", global_batch=Bg, rows_per_gpu=B,
+                                parallelism=f"rows sharded over {world} GPU(s), wcls replicated, no collective",
+                                l2="wcls 262 MB and logits > 126 MB L2; no flush"),
+                    roofline=dict(bound="tensor", achieved=achieved, peak=peak, unit="TFLOP/s",
+                                  frac=achieved / peak,
+                                  traffic=profiled_traffic("classifier_gemm_8192x4096x32000.md"),
+                                  kernel="classifier_gemm_kernel",
+                                  kernel_ms=gemm_ms, peak_source=note),
+                    cpu_baseline=None,
+                    e2e=dict(value=Bg / (e2e_ms * 1e-3), unit="tokens/s", h2d_bytes_per_step=B * D * 2,
+                             d2h_bytes_per_step=B * 4, ms_per_step=e2e_ms),
+                    gpu_launches=launches, clocks=clk)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
@@ -254,7 +385,7 @@ def run_ours(args):
             peak, peak_note = 6650.0, "of fallback"
         alg_bytes = B * VOCAB * 4 + B * (8 + 8 + 4 + 4)  # logits + state r/w + topp + ids
         achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
-        traffic = load_json(os.path.join(ROOT, "profiles", "row_sampler_traffic.json"), {}).get("bytes_per_launch")
+        traffic = profiled_traffic("row_stream_kernel_topp_4096x32000.md")
         cpu = None
         if not args.no_cpu_baseline:
             cpu = cpu_baseline(x_host, topp_host, args.cpu_rows)
@@ -287,13 +418,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--cpu-rows", type=int, default=4096)
     ap.add_argument("--ref-rows", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="topp", choices=["topp", "fused"])
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
-    return run_ours(args)
+    return run_fused(args) if args.workload == "fused" else run_ours(args)
 
 
 if __name__ == "__main__":

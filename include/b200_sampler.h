@@ -171,6 +171,13 @@ int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, c
                             unsigned long long* rng_state, int* out_ids, float* logits_out, int* row_flags,
                             void* stream);
 
+/* The classifier projection of classifier_sample_fused() alone:
+ * logits_out[b, v] = sum_k hidden[b, k] * wcls[v, k] (bf16 in, fp32 out), the
+ * batched replacement of llama2_cublas.cu:5825-5826.  Same layout rules;
+ * vocab % 32 == 0 and no upper bound on vocab.  Asynchronous on `stream`. */
+int classifier_logits(const void* hidden, const void* wcls, int batch, int dim, int vocab, float* logits_out,
+                      void* stream);
+
 /* Largest vocabulary sampler_batched_noalloc accepts. */
 #define SAMPLER_NOALLOC_MAX_VOCAB 32768
 

@@ -23,6 +23,7 @@ EXPORTED_SYMBOLS = [
     "sampler_seed_states", "sampler_last_launch_count", "sampler_last_error", "sampler_shard_rows",
     "sampler_nccl_get_unique_id", "sampler_nccl_comm_init", "sampler_nccl_allgather_ids",
     "sampler_nccl_comm_destroy", "sampler_batched_noalloc", "classifier_sample_fused",
+    "classifier_logits",
 ]
 
 
@@ -105,6 +106,8 @@ def lib():
     L.classifier_sample_fused.argtypes = [ctypes.POINTER(SamplerBatchConfig), P, P, c_int, c_int, P, P, P, P, P, P,
                                           P, P]
     L.classifier_sample_fused.restype = c_int
+    L.classifier_logits.argtypes = [P, P, c_int, c_int, c_int, P, P]
+    L.classifier_logits.restype = c_int
     _lib = L
     return L
 
@@ -194,6 +197,19 @@ def classifier_sample_fused(hidden, wcls, temperature, topp, rng_state=None, *, 
                                        _ptr(logits_out), _ptr(row_flags), _stream_ptr(stream))
     _check(rc, "classifier_sample_fused")
     return out_ids
+
+
+def classifier_logits(hidden, wcls, logits_out=None, stream=None):
+    """logits = hidden . wcls^T on the tensor cores (bf16 in, fp32 out)."""
+    import torch
+    _require_cuda(hidden, wcls, logits_out)
+    B, D = hidden.shape
+    V = wcls.shape[0]
+    if logits_out is None:
+        logits_out = torch.empty(B, V, dtype=torch.float32, device=hidden.device)
+    rc = lib().classifier_logits(_ptr(hidden), _ptr(wcls), B, D, V, _ptr(logits_out), _stream_ptr(stream))
+    _check(rc, "classifier_logits")
+    return logits_out
 
 
 def sample_batched_host(logits_np, temperature, topp, states_np, topp_rows_np=None, probs_in=False):

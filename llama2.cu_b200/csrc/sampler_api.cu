@@ -476,6 +476,36 @@ int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, c
     return rc;
 }
 
+// The classifier GEMM alone (no statistics, no sampling).
+int classifier_logits(const void* hidden, const void* wcls, int batch, int dim, int vocab, float* logits_out,
+                      void* stream) {
+    g_last_launches = 0;
+    if (!hidden || !wcls || !logits_out) return fail(SAMPLER_E_INVALID, "null hidden, wcls or logits_out");
+    if (batch < 0 || dim < 8 || (dim % 8) != 0 || vocab < 32 || (vocab % 32) != 0)
+        return fail(SAMPLER_E_INVALID, "bad sizes: batch=%d dim=%d (multiple of 8) vocab=%d (multiple of 32)", batch,
+                    dim, vocab);
+    if (((uintptr_t)hidden & 15u) || ((uintptr_t)wcls & 15u) || ((uintptr_t)logits_out & 15u))
+        return fail(SAMPLER_E_INVALID, "hidden, wcls and logits_out must be 16-byte aligned");
+    if (batch == 0) return SAMPLER_OK;
+    DeviceCtx* c = nullptr;
+    const int rc = get_ctx(&c);
+    if (rc) return rc;
+    b2s::GemmLaunch g{};
+    g.h = hidden;
+    g.w = wcls;
+    g.batch = batch;
+    g.dim = dim;
+    g.vocab = vocab;
+    g.logits = logits_out;
+    g.ld = vocab;
+    g.temperature = 1.0f;
+    g.error_word = c->error_word;
+    const int n = b2s::launch_classifier_gemm(g, c->num_sms, (cudaStream_t)stream);
+    if (n < 0) return fail(SAMPLER_E_CUDA, "classifier GEMM launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+    g_last_launches = n;
+    return SAMPLER_OK;
+}
+
 int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
                          const float* topp_rows, unsigned long long* rng_state, int* out_ids) {
     g_last_launches = 0;
