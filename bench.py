@@ -62,6 +62,15 @@ def profiled_traffic(name):
         return None
 
 
+def host_threads():
+    """Every host thread this process may use (torchrun sets
+    OMP_NUM_THREADS=1, which must not throttle the CPU baseline)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -140,10 +149,9 @@ def cpu_baseline(x, topp_rows, rows, use_ref=True, min_seconds=10.0):
     import oracle
     if use_ref and oracle.ref_available():
         lib, kind = oracle.ref_sampler(), "reference"
-        threads = lib.num_threads()
     else:
         lib, kind = oracle.oracle(), "port"
-        threads = os.cpu_count()
+    threads = host_threads()
     from __graft_entry__ import load_package
     seeds = load_package().workloads.row_seeds(rows)
     t0 = time.perf_counter()
@@ -171,7 +179,7 @@ def run_reference(args):
         oracle.build(with_ref=True)
     kind = "reference" if oracle.ref_available() else "port"
     lib = oracle.ref_sampler() if kind == "reference" else oracle.oracle()
-    threads = lib.num_threads() if kind == "reference" else os.cpu_count()
+    threads = host_threads()
     from __graft_entry__ import load_package
     seeds = load_package().workloads.row_seeds(rows)
     for _ in range(args.warmup):
@@ -387,7 +395,7 @@ def run_ours(args):
         achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
         traffic = profiled_traffic("row_stream_kernel_topp_4096x32000.md")
         cpu = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             cpu = cpu_baseline(x_host, topp_host, args.cpu_rows)
         value = world * B / (ms * 1e-3)
         line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps,
@@ -419,7 +427,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=4096)
-    ap.add_argument("--ref-rows", type=int, default=512)
+    ap.add_argument("--ref-rows", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="topp", choices=["topp", "fused"])
     args = ap.parse_args()
