@@ -58,7 +58,8 @@ constexpr int kKCap = 2048;    // nucleus keys kept on chip (more spill to L2)
 constexpr int kSideCap = 48;   // chunks whose values are kept for replays
 constexpr int kAltCap = 96;    // chunks with an alternative-binade function
 constexpr int kBinsPerThread = kBins / kST;  // 8
-constexpr int kWalkDirect = 512;  // nuclei walked element by element; larger ones by chunk functions
+constexpr int kWalkDirect = 512;
+constexpr int kPairCap = 128;   // equal-p neighbour positions recorded for the tie fix  // nuclei walked element by element; larger ones by chunk functions
 
 // chunk entry: x=L0 y=L1 z=bits(pbits | flags | alt<<8 | side<<16) w=bits(eb)
 constexpr uint32_t kFClean = 4u, kFValid = 8u, kFAlt = 16u;
@@ -82,6 +83,9 @@ struct StreamSmem {
     int n_side;
     int flag;
     int dbin;
+    int sort_next;  // next group of 32 bins to sort
+    int n_pairs;    // equal-p neighbours found by the p pass
+    int pairs[kPairCap];
     int ksel;
     int result;
     int n0;
@@ -472,6 +476,81 @@ __device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, i
     return n;
 }
 
+// Sorts every bin 0..D of the scattered nucleus by (e desc, index asc).  Warps
+// 1-7 take groups of 32 bins from a shared counter (warp 0 resolving S in the
+// meantime; having it join afterwards measured slower).  Bins of up to 16
+// keys: each key's rank is the number of
+// larger keys in its bin (keys are distinct); larger bins: bitonic networks.
+// Inside one bin (not the last) the value's top 15 bits are fixed, so 32-bit
+// keys (low 17 value bits, 0x7FFF - index) order them for V < 0x7FFF.
+__device__ void sort_bins(StreamSmem& sm, unsigned long long* kb, int D, int K, int V) {
+    const int lane = threadIdx.x & 31;
+    for (;;) {
+        int g = 0;
+        if (lane == 0) g = atomicAdd(&sm.sort_next, 1);
+        const int b0 = __shfl_sync(kFullMask, g, 0) * 32;
+        if (b0 > D) break;
+        const int b = b0 + lane;
+        int s0 = 0, n = 0;
+        if (b <= D) {
+            s0 = sm.bstart[b];
+            n = sm.hist[b] - s0;
+            if (s0 < 0 || s0 + n > K || n > 256) sm.flag = 1;
+        }
+        unsigned todo = __ballot_sync(kFullMask, n >= 2 && n <= 256 && s0 >= 0 && s0 + n <= K);
+        const unsigned small = __ballot_sync(kFullMask, n <= 16);
+        while (todo) {
+            const int src = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int ss = __shfl_sync(kFullMask, s0, src);
+            const int nn = __shfl_sync(kFullMask, n, src);
+            unsigned long long* seg = kb + ss;
+            const bool narrow = (b0 + src < kBins - 1) && V < 0x7FFF;
+            if (nn <= 16) {
+                // two small bins at a time, one per half-warp
+                const unsigned rest = todo & small;
+                const int src2 = rest ? (__ffs(rest) - 1) : -1;
+                if (src2 >= 0) todo &= ~(1u << src2);
+                const int ss2 = __shfl_sync(kFullMask, s0, src2 < 0 ? 0 : src2);
+                const int nn2 = (src2 < 0) ? 0 : __shfl_sync(kFullMask, n, src2 < 0 ? 0 : src2);
+                const bool narrow2 = narrow && (src2 < 0 || b0 + src2 < kBins - 1);
+                const int hl = lane & 15;
+                const int my_ss = (lane < 16) ? ss : ss2;
+                const int my_nn = (lane < 16) ? nn : nn2;
+                const unsigned long long key = (hl < my_nn) ? kb[my_ss + hl] : 0ull;
+                const int top = max(nn, nn2);
+                int rank = 0;
+                if (narrow2) {
+                    const uint32_t vb = (uint32_t)(key >> 32);
+                    const uint32_t k32 = ((vb & 0x1FFFFu) << 15) | (uint32_t)(0x7FFF - key_index(key));
+                    for (int t = 0; t < top; ++t) {
+                        const uint32_t o = __shfl_sync(kFullMask, k32, (lane & 16) | t);
+                        rank += (t < my_nn && o > k32) ? 1 : 0;
+                    }
+                } else {
+                    for (int t = 0; t < top; ++t) {
+                        const unsigned long long o = __shfl_sync(kFullMask, key, (lane & 16) | t);
+                        rank += (t < my_nn && o > key) ? 1 : 0;
+                    }
+                }
+                __syncwarp();
+                if (hl < my_nn) kb[my_ss + rank] = key;
+                __syncwarp();
+            } else if (narrow) {
+                if (nn <= 32) warp_sort_bin<1>(seg, nn, lane);
+                else if (nn <= 64) warp_sort_bin<2>(seg, nn, lane);
+                else if (nn <= 128) warp_sort_bin<4>(seg, nn, lane);
+                else warp_sort_bin<8>(seg, nn, lane);
+            } else {
+                if (nn <= 32) warp_sort_desc<1>(seg, nn, lane);
+                else if (nn <= 64) warp_sort_desc<2>(seg, nn, lane);
+                else if (nn <= 128) warp_sort_desc<4>(seg, nn, lane);
+                else warp_sort_desc<8>(seg, nn, lane);
+            }
+        }
+    }
+}
+
 __device__ void defer_row_s(const RowLaunch& p, int row) {
     const int k = atomicAdd(p.defer_count, 1);
     p.defer_rows[k] = row;
@@ -677,6 +756,7 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
             sm.n_side = 0;
             sm.flag = 0;
             sm.dbin = -1;
+            sm.sort_next = 0;
         }
         for (int b = tid; b < kBins; b += kST) sm.hist[b] = 0;
         __syncthreads();
@@ -914,36 +994,7 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                     }
                 }
                 named_bar(1, kST - 32);
-                // sort the bins holding two or more elements: warp w takes
-                // the groups of 32 bins w-1, w-1+7, ...
-                for (int b0 = (warp - 1) * 32; b0 <= D; b0 += (kSW - 1) * 32) {
-                    const int b = b0 + lane;
-                    int s0 = 0, n = 0;
-                    if (b <= D) {
-                        s0 = sm.bstart[b];
-                        n = sm.hist[b] - s0;
-                        if (s0 < 0 || s0 + n > K || n > 256) sm.flag = 1;
-                    }
-                    unsigned todo = __ballot_sync(kFullMask, n >= 2 && n <= 256 && s0 >= 0 && s0 + n <= K);
-                    while (todo) {
-                        const int src = __ffs(todo) - 1;
-                        todo &= todo - 1;
-                        const int ss = __shfl_sync(kFullMask, s0, src);
-                        const int nn = __shfl_sync(kFullMask, n, src);
-                        unsigned long long* seg = kb + ss;
-                        if (b0 + src < kBins - 1 && V < 0x7FFF) {
-                            if (nn <= 32) warp_sort_bin<1>(seg, nn, lane);
-                            else if (nn <= 64) warp_sort_bin<2>(seg, nn, lane);
-                            else if (nn <= 128) warp_sort_bin<4>(seg, nn, lane);
-                            else warp_sort_bin<8>(seg, nn, lane);
-                        } else {
-                            if (nn <= 32) warp_sort_desc<1>(seg, nn, lane);
-                            else if (nn <= 64) warp_sort_desc<2>(seg, nn, lane);
-                            else if (nn <= 128) warp_sort_desc<4>(seg, nn, lane);
-                            else warp_sort_desc<8>(seg, nn, lane);
-                        }
-                    }
-                }
+                sort_bins(sm, kb, D, K, V);
             }
             __syncthreads();
             const float S = sm.fval;
@@ -960,9 +1011,11 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                     const float q = __fmul_rn(e, rS);
                     return __fmaf_rn(__fmaf_rn(-q, S, e), rS, q);
                 };
-                if (tid == 0) sm.n0 = 0;
+                if (tid == 0) {
+                    sm.n0 = 0;
+                    sm.n_pairs = 0;
+                }
                 __syncthreads();
-                bool any_run = false;
                 for (int base = 0; base < K; base += 4 * kST) {  // uniform trip count (barrier inside)
                     const int i0 = base + tid;
                     unsigned long long k[4], kn[4];
@@ -979,7 +1032,10 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                             const float pv = to_p(key_prob(k[u]));
                             const bool has_next = i + 1 < K;
                             const float pn = has_next ? to_p(key_prob(kn[u])) : -1.0f;
-                            any_run |= (pn == pv);
+                            if (pn == pv) {
+                                const int q = atomicAdd(&sm.n_pairs, 1);
+                                if (q < kPairCap) sm.pairs[q] = i;
+                            }
                             if (pv >= cutoff && !(pn >= cutoff)) sm.n0 = i + 1;
                             k[u] = ((unsigned long long)__float_as_uint(pv) << 32) | (k[u] & 0xFFFFFFFFull);
                         }
@@ -990,9 +1046,15 @@ __global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
                         if (i0 + u * kST < K) kb[i0 + u * kST] = k[u];
                 }
                 // equal-p runs (sorted by e, so contiguous) go to index order,
-                // glibc qsort's order for ties (rare: runs are a few keys)
-                if (__syncthreads_or(any_run)) {
-                    for (int i = tid; i + 1 < K; i += kST) {
+                // glibc qsort's order for ties; runs are a few keys, found from
+                // the recorded neighbour pairs (all positions if too many)
+                __syncthreads();
+                const int npairs = sm.n_pairs;
+                if (npairs > 0) {
+                    const bool listed = npairs <= kPairCap;
+                    const int nscan = listed ? npairs : K - 1;
+                    for (int q = tid; q < nscan; q += kST) {
+                        const int i = listed ? sm.pairs[q] : q;
                         const unsigned long long a = kb[i];
                         if ((a >> 32) == (kb[i + 1] >> 32) && (i == 0 || (kb[i - 1] >> 32) != (a >> 32))) {
                             int j = i + 1;
