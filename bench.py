@@ -21,6 +21,12 @@ projection of B = 8192 bf16 hidden states (dim 4096, sharded over the GPUs)
 against a bf16 wcls [32000, 4096] on the tensor cores, then top-p sampling
 (T = 0.8, topp 0.9) of the resulting rows; its roofline is the GEMM kernel
 against the measured bf16 tensor peak.
+
+`--workload decode` measures one decode step at batch 1 (latency): the
+classifier projection of one hidden state plus sampling, ours
+(`classifier_sample_fused`, bf16 wcls, id read back to the host) against the
+reference's step (fp32 cuBLAS GEMV of wcls as `llama2_cublas.cu:5825-5826`,
+the 128 KB logits copied to the host, its own sample() on the host).
 """
 import argparse
 import json
@@ -304,6 +310,64 @@ def run_fused(args):
     return 0
 
 
+def run_decode(args):
+    """Batch-1 decode step latency, greedy and top-p, ours vs the reference's path."""
+    import torch
+    import oracle
+    from __graft_entry__ import load_package
+    pkg = load_package()
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    f = pkg.workloads.fused(rows=1)
+    D, V = f["hidden"].shape[1], f["wcls"].shape[0]
+    h = torch.from_numpy(f["hidden"].view(np.int16)).view(torch.bfloat16).to(dev)
+    w = torch.from_numpy(f["wcls"].view(np.int16)).view(torch.bfloat16).to(dev)
+    w32 = w.float()
+    h32 = h.float()[0]
+    if not oracle.ref_available():
+        oracle.build(with_ref=True)
+    ref = oracle.ref_sampler() if oracle.ref_available() else oracle.oracle()
+    kind = "reference" if oracle.ref_available() else "port"
+    st = torch.empty(1, dtype=torch.int64, device=dev)
+    ids = torch.empty(1, dtype=torch.int32, device=dev)
+    ids_host = torch.empty(1, dtype=torch.int32).pin_memory()
+    logits_host = torch.empty(V, dtype=torch.float32).pin_memory()
+    out = {}
+    for temp in (0.0, f["temperature"]):
+        def ours():
+            pkg.seed_states(st, f["seed"])
+            pkg.classifier_sample_fused(h, w, temp, f["topp"], st, out_ids=ids)
+            ids_host.copy_(ids)
+            return int(ids_host[0])
+
+        def reference():
+            lg = torch.mv(w32, h32)
+            logits_host.copy_(lg)
+            ids_r = ref.sample_batch(logits_host.numpy()[None, :], temp, f["topp"],
+                                     np.array([f["seed"]], np.uint64), nthreads=1)[0]
+            return int(ids_r[0])
+
+        res = {}
+        for name, fn in (("ours", ours), ("reference_path", reference)):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                fn()
+            res[name] = (time.perf_counter() - t0) / args.steps * 1e6
+        out["greedy" if temp == 0.0 else "topp"] = dict(ours_us=res["ours"], reference_path_us=res["reference_path"])
+    line = dict(metric="decode step latency at batch 1 (classifier + sampling), us", value=out["topp"]["ours_us"],
+                unit="us", n_gpus=1, steps=args.steps, warmup=args.warmup, higher_is_better=False,
+                vs_baseline=None, dtype="bf16", data="synthetic (seeded numpy PCG64)",
+                config=dict(workload=f"decode: hidden bf16 [1,{D}] x wcls [{V},{D}], T={f['temperature']}, "
+                                     f"topp {f['topp']}; greedy T=0"),
+                latency=out, reference_kind=kind,
+                reference_path="torch.mv fp32 wcls (cuBLAS GEMV) + 128 KB D2H + reference sample() on one host thread")
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -429,10 +493,12 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4096)
     ap.add_argument("--ref-rows", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="topp", choices=["topp", "fused"])
+    ap.add_argument("--workload", default="topp", choices=["topp", "fused", "decode"])
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "decode":
+        return run_decode(args)
     return run_fused(args) if args.workload == "fused" else run_ours(args)
 
 
