@@ -69,7 +69,6 @@ struct StreamSmem {
     int hist[kBins];
     unsigned short bstart[kBins];  // bin offsets in the nucleus (< 2^16)
     float side[kSideCap][kSC];
-    float replay[kSC];
     float4 fn[kChunks];
     float4 alt[kAltCap];
     float4 wfn[kSegs];
@@ -255,22 +254,22 @@ __device__ __forceinline__ float exact_e(const Ctx& c, const StreamSmem& sm, flo
 }
 
 // Replays chunk t exactly starting from s (warp 0): kept values, or values
-// recomputed from the row (no absorption) into the replay scratch.
+// recomputed from the row.  A replayed chunk is one whose running sum crosses
+// a binade (often several, early in the row), so the 32 adds are done
+// serially -- redundantly in every lane -- rather than by the warp-parallel
+// chain, whose steps end at every crossing.
 __device__ float replay_chunk(StreamSmem& sm, const Ctx& c, int t, uint32_t side_plus1, float s) {
     const int lane = threadIdx.x & 31;
     const int base = t * kSC;
     const int cnt = min(kSC, c.V - base);
     if (side_plus1) {
         const float* vals = sm.side[side_plus1 - 1];
-        warp_chain([&](int i) { return vals[i]; }, cnt, s, INFINITY);
+#pragma unroll 8
+        for (int i = 0; i < cnt; ++i) s = __fadd_rn(s, vals[i]);
         return s;
     }
-    float* scratch = sm.replay;  // warp 0's own: the other warps fill kbuf meanwhile
     const float e = (lane < cnt) ? exact_e(c, sm, __ldg(c.src + base + lane)) : 0.0f;
-    scratch[lane] = e;
-    __syncwarp();
-    warp_chain([&](int i) { return scratch[i]; }, cnt, s, INFINITY);
-    __syncwarp();
+    for (int i = 0; i < cnt; ++i) s = __fadd_rn(s, __shfl_sync(kFullMask, e, i));
     return s;
 }
 
@@ -463,10 +462,14 @@ __device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, i
             if (cpos < cnt) {
                 const int base = (seg * 32 + cpos) * kSC;
                 const int ne = min(kSC, n - base);
-                const int k = warp_chain([&](int i) { return key_prob(kb[base + i]); }, ne, s, theta);
-                if (k < ne) {
-                    cum = s;
-                    return base + k;
+                // the crossing chunk: 32 serial adds (one coalesced load, shuffles)
+                const float x = (lane < ne) ? key_prob(kb[base + lane]) : 0.0f;
+                for (int i = 0; i < ne; ++i) {
+                    s = __fadd_rn(s, __shfl_sync(kFullMask, x, i));
+                    if (s > theta) {
+                        cum = s;
+                        return base + i;
+                    }
                 }
                 ++cpos;
             }
