@@ -178,6 +178,20 @@ int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, c
 int classifier_logits(const void* hidden, const void* wcls, int batch, int dim, int vocab, float* logits_out,
                       void* stream);
 
+/* The final RMSNorm of the last layer's output (llama2.c:422-433 rmsnorm,
+ * applied at llama2_cublas.cu:5809-5815) as the classifier's prologue:
+ * out_bf16[b, j] = bf16(norm_weight[j] * (x[b, j] / sqrt(mean_j(x[b, :]^2) + 1e-5)))
+ * for fp32 x [batch, dim] and norm_weight [dim]; device buffers. */
+int rmsnorm_bf16(const float* x, const float* norm_weight, int batch, int dim, void* out_bf16, void* stream);
+
+/* The whole decode step from the last layer's fp32 output: rmsnorm_bf16 into
+ * a library-managed buffer, then classifier_sample_fused (same arguments and
+ * results). */
+int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* x, const float* norm_weight,
+                                    const void* wcls, int batch, int dim, const float* temperature_rows,
+                                    const float* topp_rows, const float* coins, unsigned long long* rng_state,
+                                    int* out_ids, float* logits_out, int* row_flags, void* stream);
+
 /* Largest vocabulary sampler_batched_noalloc accepts. */
 #define SAMPLER_NOALLOC_MAX_VOCAB 32768
 

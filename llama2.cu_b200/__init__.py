@@ -23,7 +23,7 @@ EXPORTED_SYMBOLS = [
     "sampler_seed_states", "sampler_last_launch_count", "sampler_last_error", "sampler_shard_rows",
     "sampler_nccl_get_unique_id", "sampler_nccl_comm_init", "sampler_nccl_allgather_ids",
     "sampler_nccl_comm_destroy", "sampler_batched_noalloc", "classifier_sample_fused",
-    "classifier_logits",
+    "classifier_logits", "rmsnorm_bf16", "classifier_rmsnorm_sample_fused",
 ]
 
 
@@ -108,6 +108,11 @@ def lib():
     L.classifier_sample_fused.restype = c_int
     L.classifier_logits.argtypes = [P, P, c_int, c_int, c_int, P, P]
     L.classifier_logits.restype = c_int
+    L.rmsnorm_bf16.argtypes = [P, P, c_int, c_int, P, P]
+    L.rmsnorm_bf16.restype = c_int
+    L.classifier_rmsnorm_sample_fused.argtypes = [ctypes.POINTER(SamplerBatchConfig), P, P, P, c_int, c_int, P, P,
+                                                  P, P, P, P, P, P]
+    L.classifier_rmsnorm_sample_fused.restype = c_int
     _lib = L
     return L
 
@@ -210,6 +215,39 @@ def classifier_logits(hidden, wcls, logits_out=None, stream=None):
     rc = lib().classifier_logits(_ptr(hidden), _ptr(wcls), B, D, V, _ptr(logits_out), _stream_ptr(stream))
     _check(rc, "classifier_logits")
     return logits_out
+
+
+def rmsnorm_bf16(x, norm_weight, out=None, stream=None):
+    """bf16(norm_weight * x / rms(x)) per row of a float32 CUDA tensor [B, D]."""
+    import torch
+    _require_cuda(x, norm_weight, out)
+    B, D = x.shape
+    if out is None:
+        out = torch.empty(B, D, dtype=torch.bfloat16, device=x.device)
+    _check(lib().rmsnorm_bf16(_ptr(x), _ptr(norm_weight), B, D, _ptr(out), _stream_ptr(stream)), "rmsnorm_bf16")
+    return out
+
+
+def classifier_rmsnorm_sample_fused(x, norm_weight, wcls, temperature, topp, rng_state=None, *,
+                                    temperature_rows=None, topp_rows=None, coins=None, out_ids=None,
+                                    logits_out=None, row_flags=None, stream=None):
+    """Decode step from fp32 hidden states [B, D]: final RMSNorm, classifier
+    GEMM, sampling.  Returns out_ids (int32 CUDA tensor [B])."""
+    import torch
+    _require_cuda(x, norm_weight, wcls, rng_state, temperature_rows, topp_rows, coins, logits_out, row_flags)
+    if x.dtype != torch.float32 or not x.is_contiguous() or wcls.dtype != torch.bfloat16:
+        raise SamplerError("x must be contiguous float32 [B, D] and wcls bfloat16 [V, D]")
+    B, D = x.shape
+    V = wcls.shape[0]
+    if out_ids is None:
+        out_ids = torch.empty(B, dtype=torch.int32, device=x.device)
+    cfg = SamplerBatchConfig(V, float(temperature), float(topp), 0)
+    rc = lib().classifier_rmsnorm_sample_fused(ctypes.byref(cfg), _ptr(x), _ptr(norm_weight), _ptr(wcls), B, D,
+                                               _ptr(temperature_rows), _ptr(topp_rows), _ptr(coins),
+                                               _ptr(rng_state), _ptr(out_ids), _ptr(logits_out), _ptr(row_flags),
+                                               _stream_ptr(stream))
+    _check(rc, "classifier_rmsnorm_sample_fused")
+    return out_ids
 
 
 def sample_batched_host(logits_np, temperature, topp, states_np, topp_rows_np=None, probs_in=False):

@@ -26,6 +26,7 @@
 #include "sampler_kernels.cuh"
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -346,7 +347,40 @@ bool make_tmap(CUtensorMap* m, const void* base, int rows, int dim, int box_rows
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// ---- final RMSNorm prologue ---------------------------------------------------
+// o = weight * (x * 1/sqrt(mean(x^2) + 1e-5)) per row (the reference's
+// rmsnorm, llama2.c:422-433, applied to the final hidden state at
+// llama2_cublas.cu:5809-5815), rounded to bf16: the classifier GEMM's A
+// operand.  One 256-thread CTA per row; the sum of squares is a tree sum
+// (the reference's is serial), so o can differ from the reference's in the
+// last bit of the fp32 value before the bf16 rounding.
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_bf16_kernel(const float* x, const float* w, int dim,
+                                                                    __nv_bfloat16* out) {
+    __shared__ float red[kNormThreads / 32];
+    const float* xr = x + (long long)blockIdx.x * dim;
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < dim; j += kNormThreads) ss = __fmaf_rn(xr[j], xr[j], ss);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(kFullMask, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)dim), 1e-5f)));
+    __nv_bfloat16* orow = out + (long long)blockIdx.x * dim;
+    for (int j = threadIdx.x; j < dim; j += kNormThreads) orow[j] = __float2bfloat16_rn(__fmul_rn(w[j], __fmul_rn(r, xr[j])));
+}
+
 }  // namespace
+
+int launch_rmsnorm_bf16(const float* x, const float* weight, int batch, int dim, void* out, cudaStream_t stream) {
+    rmsnorm_bf16_kernel<<<batch, kNormThreads, 0, stream>>>(x, weight, dim, static_cast<__nv_bfloat16*>(out));
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 1 : -(int)e;
+}
 
 size_t gemm_smem_bytes() { return kGemmSmemBytes; }
 

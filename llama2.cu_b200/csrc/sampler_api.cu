@@ -76,6 +76,8 @@ struct DeviceCtx {
     size_t flogits_cap = 0;
     float4* d_stats = nullptr;
     size_t stats_cap = 0;
+    void* d_hnorm = nullptr;  // bf16 normalized hidden states
+    size_t hnorm_cap = 0;
 };
 
 std::mutex g_mu;
@@ -472,6 +474,52 @@ int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, c
     if (n < 0) return fail(SAMPLER_E_CUDA, "classifier GEMM launch: %s", cudaGetErrorString((cudaError_t)(-n)));
     rc = dispatch(cfg, logits, batch, V, temperature_rows, topp_rows, coins, rng_state, out_ids, nullptr, row_flags,
                   nullptr, 0, (cudaStream_t)stream, 0, stats, sld);
+    g_last_launches += n;
+    return rc;
+}
+
+// Final RMSNorm prologue alone: out_bf16[b, :] = bf16(weight * (x[b, :] / rms)).
+int rmsnorm_bf16(const float* x, const float* norm_weight, int batch, int dim, void* out_bf16, void* stream) {
+    g_last_launches = 0;
+    if (!x || !norm_weight || !out_bf16) return fail(SAMPLER_E_INVALID, "null x, norm_weight or out_bf16");
+    if (batch < 0 || dim < 1) return fail(SAMPLER_E_INVALID, "bad sizes: batch=%d dim=%d", batch, dim);
+    if (batch == 0) return SAMPLER_OK;
+    const int n = b2s::launch_rmsnorm_bf16(x, norm_weight, batch, dim, out_bf16, (cudaStream_t)stream);
+    if (n < 0) return fail(SAMPLER_E_CUDA, "rmsnorm launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+    g_last_launches = n;
+    return SAMPLER_OK;
+}
+
+// The decode step from the last layer's fp32 output: final RMSNorm, classifier
+// GEMM with the statistics epilogue, sampling.
+int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* x, const float* norm_weight,
+                                    const void* wcls, int batch, int dim, const float* temperature_rows,
+                                    const float* topp_rows, const float* coins, unsigned long long* rng_state,
+                                    int* out_ids, float* logits_out, int* row_flags, void* stream) {
+    g_last_launches = 0;
+    if (!x || !norm_weight) return fail(SAMPLER_E_INVALID, "null x or norm_weight");
+    if (batch < 0 || dim < 8 || (dim % 8) != 0) return fail(SAMPLER_E_INVALID, "bad sizes: batch=%d dim=%d", batch, dim);
+    if (batch == 0) return SAMPLER_OK;
+    DeviceCtx* c = nullptr;
+    int rc = get_ctx(&c);
+    if (rc) return rc;
+    const size_t need = (size_t)batch * (size_t)dim * 2;
+    void* h = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (c->hnorm_cap < need) {
+            if (c->d_hnorm) cudaFree(c->d_hnorm);
+            c->d_hnorm = nullptr;
+            c->hnorm_cap = 0;
+            B2S_CUDA(cudaMalloc(&c->d_hnorm, need));
+            c->hnorm_cap = need;
+        }
+        h = c->d_hnorm;
+    }
+    const int n = b2s::launch_rmsnorm_bf16(x, norm_weight, batch, dim, h, (cudaStream_t)stream);
+    if (n < 0) return fail(SAMPLER_E_CUDA, "rmsnorm launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+    rc = classifier_sample_fused(cfg, h, wcls, batch, dim, temperature_rows, topp_rows, coins, rng_state, out_ids,
+                                 logits_out, row_flags, stream);
     g_last_launches += n;
     return rc;
 }

@@ -7,7 +7,9 @@ Bars:
     plus LOGIT_RTOL times the sum of |products| of the entry;
   * ids, states and flags: identical to sampler_batched() run on the fused
     call's own logits (the epilogue statistics only replace the sampler's
-    first pass), and those ids pass the end-to-end rule against the oracle.
+    first pass), and those ids pass the end-to-end rule against the oracle;
+  * the final RMSNorm prologue: within one bf16 rounding of a PyTorch fp32
+    rmsnorm (the sum of squares is a tree sum here, serial in the reference).
 """
 import numpy as np
 import pytest
@@ -112,3 +114,30 @@ def test_fused_rejects_bad_shapes(pkg):
     h, w = operands(4, 64, 100, seed=1)  # vocab not a multiple of 32
     with pytest.raises(pkg.SamplerError):
         pkg.classifier_sample_fused(h, w, 1.0, 0.9, torch.zeros(4, dtype=torch.int64, device=DEV))
+
+
+def test_rmsnorm_prologue_and_decode_step(pkg):
+    """Final RMSNorm (llama2.c rmsnorm) into bf16, then the fused classifier:
+    the normalized rows are within one bf16 rounding of a PyTorch fp32
+    reference, and the decode step's ids equal classifier_sample_fused on
+    those rows."""
+    B, D, V = 96, 4096, 32000
+    g = torch.Generator().manual_seed(31)
+    x = (torch.randn(B, D, generator=g) * 3.0).to(DEV)
+    nw = (1.0 + 0.1 * torch.randn(D, generator=g)).to(DEV)
+    w = (torch.randn(V, D, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    h = pkg.rmsnorm_bf16(x, nw)
+    torch.cuda.synchronize()
+    ref = nw * (x * (1.0 / torch.sqrt((x * x).mean(dim=1, keepdim=True) + 1e-5)))
+    ref_b = ref.to(torch.bfloat16).float()
+    diff = (h.float() - ref_b).abs()
+    ulp = ref_b.abs() * 2.0 ** -7  # one bf16 ulp (8-bit significand)
+    assert bool((diff <= ulp + 1e-30).all()), f"max diff {diff.max().item():.3g}"
+    assert float((diff == 0).float().mean()) > 0.999  # nearly all bit-identical
+    seeds = pkg.workloads.row_seeds(B)
+    st1 = torch.from_numpy(seeds.view(np.int64).copy()).to(DEV)
+    st2 = st1.clone()
+    ids1 = pkg.classifier_rmsnorm_sample_fused(x, nw, w, 0.8, 0.9, st1)
+    ids2 = pkg.classifier_sample_fused(h, w, 0.8, 0.9, st2)
+    torch.cuda.synchronize()
+    assert torch.equal(ids1, ids2) and torch.equal(st1, st2)
