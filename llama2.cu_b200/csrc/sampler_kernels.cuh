@@ -83,6 +83,8 @@ int stream_ctas_per_sm();
 int launch_row_stream(const RowLaunch& p, int num_ctas, cudaStream_t stream);
 // Persistent tcgen05 GEMM, one CTA per SM (at most num_sms CTAs).
 int launch_classifier_gemm(const GemmLaunch& p, int num_sms, cudaStream_t stream);
+// The same GEMM by CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles).
+int launch_classifier_gemm_pair(const GemmLaunch& p, int num_sms, cudaStream_t stream);
 size_t gemm_smem_bytes();
 // Final RMSNorm of `batch` fp32 rows into bf16 (the GEMM's A operand).
 int launch_rmsnorm_bf16(const float* x, const float* weight, int batch, int dim, void* out, cudaStream_t stream);
