@@ -297,7 +297,7 @@ def run_fused(args):
                     roofline=dict(bound="tensor", achieved=achieved, peak=peak, unit="TFLOP/s",
                                   frac=achieved / peak,
                                   traffic=profiled_traffic("classifier_gemm_8192x4096x32000.md"),
-                                  kernel="classifier_gemm_kernel",
+                                  kernel="classifier_gemm_pair_kernel",
                                   kernel_ms=gemm_ms, peak_source=note),
                     cpu_baseline=None,
                     e2e=dict(value=Bg / (e2e_ms * 1e-3), unit="tokens/s", h2d_bytes_per_step=B * D * 2,

@@ -1,11 +1,14 @@
 // row_stream.cu -- the streaming top-p kernel (the fast path for sample()).
 //
-// Four 256-thread CTAs per SM, each owning one row at a time (persistent
-// grid).  While one CTA is in a sequential phase (the exact serial-sum
-// resolution, the nucleus walk), the other CTAs on the SM keep its pipes and
-// the HBM busy.  The row (V <= 32768) is walked in four strips of 8192
-// elements; in strip s thread t owns the 32-element chunk 256s + t, loaded
-// with eight independent 16-byte loads.
+// Two CTA shapes, both persistent with one row per CTA at a time.  Batches
+// larger than the SM count: four 256-thread CTAs per SM -- while one CTA is
+// in a sequential phase (the exact serial-sum resolution, the nucleus walk),
+// the other CTAs on the SM keep its pipes and the HBM busy; the row
+// (V <= 32768, 1024 chunks of 32) is walked in four strips, thread t owning
+// chunk 256s + t of strip s.  Batches up to the SM count (decode): one
+// 1024-thread CTA per SM, one chunk per thread, so each row's parallel
+// phases use a whole SM.  Chunks are loaded with eight independent 16-byte
+// loads.
 //
 //   Pass 1 (HBM read): max/min of the logits and, per chunk, an approximate
 //     online sum of exp(x - max) (ex2.approx) -- used to guess which binade
@@ -14,8 +17,7 @@
 //     thread): x = l/T (Markstein division) and d = x - max.  An element
 //     whose e = exp(d) is provably below half an ulp of the (guessed) running
 //     sum is absorbed by the serial fp32 sum -- llama2.c's loop adds it and
-//     nothing changes -- so its exact e is never needed: e = 0 stands in for
-//     it.  Everything else gets the exact table-driven exp.  The binade-chain
+//     nothing changes.  Every element gets the exact table-driven exp.  The binade-chain
 //     function of the chunk is built on the fly (exact_math.cuh), plus an
 //     alternative for the neighbouring binade when the guess lies near a
 //     boundary.  Possible top-p candidates (e >= cutoff*S_approx, with margin)
@@ -46,1103 +48,30 @@
 #include <atomic>
 
 namespace b2s {
-namespace {
 
-constexpr int kST = 256;       // threads per CTA
-constexpr int kSW = kST / 32;  // warps per CTA
-constexpr int kSC = 32;        // elements per chunk
-constexpr int kStrips = 4;     // chunks per thread (strip s: chunk 256s + t)
-constexpr int kChunks = kST * kStrips;      // 1024 chunks of 32 (V <= 32768)
-constexpr int kSegs = kChunks / 32;         // 32 segments of 32 chunks
-constexpr int kKCap = 2048;    // nucleus keys kept on chip (more spill to L2)
-constexpr int kSideCap = 48;   // chunks whose values are kept for replays
-constexpr int kAltCap = 96;    // chunks with an alternative-binade function
-constexpr int kBinsPerThread = kBins / kST;  // 8
-constexpr int kWalkDirect = 512;
-constexpr int kPairCap = 128;   // equal-p neighbour positions recorded for the tie fix  // nuclei walked element by element; larger ones by chunk functions
+#define RS_THREADS 256
+#define RS_CTAS_PER_SM 4
+#define RS_NS rs256
+#include "row_stream_impl.cuh"
+#undef RS_NS
+#undef RS_CTAS_PER_SM
+#undef RS_THREADS
 
-// chunk entry: x=L0 y=L1 z=bits(pbits | flags | alt<<8 | side<<16) w=bits(eb)
-constexpr uint32_t kFClean = 4u, kFValid = 8u, kFAlt = 16u;
+#define RS_THREADS 1024
+#define RS_CTAS_PER_SM 1
+#define RS_NS rs1024
+#include "row_stream_impl.cuh"
+#undef RS_NS
+#undef RS_CTAS_PER_SM
+#undef RS_THREADS
 
-struct StreamSmem {
-    unsigned long long kbuf[kKCap];
-    int hist[kBins];
-    unsigned short bstart[kBins];  // bin offsets in the nucleus (< 2^16)
-    float side[kSideCap][kSC];
-    float4 fn[kChunks];
-    float4 alt[kAltCap];
-    float4 wfn[kSegs];
-    xm::ExpTableEntry exptab[xm::kExpTableSize];
-    float red_a[kSW];
-    float red_b[kSW];
-    float red_c[kSW];
-    float red_s[kStrips][kSW];
-    int red_i[kSW];
-    int n_alt;
-    int n_side;
-    int flag;
-    int dbin;
-    int sort_next;  // next group of 32 bins to sort
-    int n_pairs;    // equal-p neighbours found by the p pass
-    int pairs[kPairCap];
-    int ksel;
-    int result;
-    int n0;
-    float fval;
-};
-
-// Four CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per CTA.
-static_assert(4 * (sizeof(StreamSmem) + 1024) <= 228 * 1024, "StreamSmem too large for 4 CTAs per SM");
-
-struct Ctx {
-    const float* src;  // row
-    int V;
-    int nch;
-    float T, rT;
-    float max_x;
-    bool unit;
-};
-
-// ---------------------------------------------------------------------------
-// block helpers (256 threads)
-// ---------------------------------------------------------------------------
-struct ScanF {
-    float incl, excl, total;
-};
-
-// Float scan whose exclusive value of thread t+1 is bitwise the inclusive
-// value of thread t, so "excl < x <= incl" selects exactly one thread.
-__device__ ScanF block_scan_f(float v, StreamSmem& sm) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(kFullMask, v, o);
-        if (lane >= o) v += y;
-    }
-    const float e = __shfl_up_sync(kFullMask, v, 1);
-    if (lane == 31) sm.red_a[warp] = v;
-    __syncthreads();
-    float p = 0.0f, t = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kSW; ++w) {
-        const float x = sm.red_a[w];
-        if (w < warp) p += x;
-        t += x;
-    }
-    __syncthreads();
-    ScanF r;
-    r.incl = p + v;
-    r.excl = lane == 0 ? p : p + e;
-    r.total = t;
-    return r;
-}
-
-__device__ int block_scan_i(int v, StreamSmem& sm, int& total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(kFullMask, v, o);
-        if (lane >= o) v += y;
-    }
-    if (lane == 31) sm.red_i[warp] = v;
-    __syncthreads();
-    int p = 0, t = 0;
-#pragma unroll
-    for (int w = 0; w < kSW; ++w) {
-        const int x = sm.red_i[w];
-        if (w < warp) p += x;
-        t += x;
-    }
-    __syncthreads();
-    total = t;
-    return p + v;
-}
-
-__device__ __forceinline__ xm::ChainFn fn_shfl_up(const xm::ChainFn& f, int o) {
-    return xm::ChainFn{__shfl_up_sync(kFullMask, f.L0, o), __shfl_up_sync(kFullMask, f.L1, o),
-                       __shfl_up_sync(kFullMask, f.pbits, o)};
-}
-__device__ __forceinline__ xm::ChainFn warp_incl_compose(xm::ChainFn f) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const xm::ChainFn y = fn_shfl_up(f, o);
-        if (lane >= o) f = xm::chain_compose(y, f);
-    }
-    return f;
-}
-
-__device__ __forceinline__ bool regular_sum(float s) {
-    const uint32_t eb = xm::binade_of(s);
-    return s > 0.0f && eb >= xm::kMinFastBinade && eb < 254u;
-}
-
-// ---------------------------------------------------------------------------
-// Warp-cooperative exact serial sum: s_i = fl(s_{i-1} + a_i) over i < n,
-// starting from the exact value s.  Returns the first i with s_i > theta
-// (s = s_i), or n (s = s_{n-1}).  While s is a normal number well above
-// 2^-100, 32 addends are handled per step: each lane forms its addend's
-// chain function in the binade of s, an inclusive warp scan composes them,
-// and every lane whose running sum stays in that binade is exact; the addend
-// that leaves the binade is added for real.  Addends must be >= 0.
-// ---------------------------------------------------------------------------
-template <class Get>
-__device__ int warp_chain(const Get& get, int n, float& s, float theta) {
-    const int lane = threadIdx.x & 31;
-    int pos = 0;
-    while (pos < n) {
-        const int i = pos + lane;
-        const float x = (i < n) ? get(i) : 0.0f;
-        if (regular_sum(s)) {
-            const uint32_t sb = __float_as_uint(s);
-            const uint32_t eb = (sb >> 23) & 0xFFu;
-            const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
-            const float v0 = __fadd_rn(lo, x), v1 = __fadd_rn(lo1, x);
-            const bool ok = (i < n) && ((__float_as_uint(v0) >> 23) == eb) && ((__float_as_uint(v1) >> 23) == eb);
-            xm::ChainFn f = ok ? xm::ChainFn{__fsub_rn(v0, lo), __fsub_rn(v1, lo1),
-                                             (__float_as_uint(v0) & 1u) | ((__float_as_uint(v1) & 1u) << 1)}
-                               : xm::chain_identity();
-            const unsigned okm = __ballot_sync(kFullMask, ok);
-            const int fi = (~okm) ? (__ffs(~okm) - 1) : 32;
-            f = warp_incl_compose(f);
-            const float hi = __uint_as_float((eb + 1u) << 23);
-            const float L = (sb & 1u) ? f.L1 : f.L0;
-            const bool inb = (lane < fi) && (L <= __fsub_rn(hi, s));
-            const unsigned inm = __ballot_sync(kFullMask, inb);
-            const int m = (~inm) ? (__ffs(~inm) - 1) : 32;
-            const float sl = __fadd_rn(s, L);
-            const unsigned hit = __ballot_sync(kFullMask, (lane < m) && (sl > theta));
-            if (hit) {
-                const int h = __ffs(hit) - 1;
-                s = __shfl_sync(kFullMask, sl, h);
-                return pos + h;
-            }
-            if (m > 0) s = __shfl_sync(kFullMask, sl, m - 1);
-            const float a = __shfl_sync(kFullMask, x, m & 31);
-            pos += m;
-            if (m < 32 && pos < n) {
-                s = __fadd_rn(s, a);
-                if (s > theta) return pos;
-                pos += 1;
-            }
-        } else if (s == 0.0f) {
-            const unsigned nz = __ballot_sync(kFullMask, (i < n) && (x != 0.0f));
-            if (!nz) {
-                pos += 32;
-                continue;
-            }
-            const int z = __ffs(nz) - 1;
-            const float a = __shfl_sync(kFullMask, x, z);
-            pos += z;
-            s = __fadd_rn(s, a);
-            if (s > theta) return pos;
-            pos += 1;
-        } else {
-            const float a = __shfl_sync(kFullMask, x, 0);
-            s = __fadd_rn(s, a);
-            if (s > theta) return pos;
-            pos += 1;
-        }
-    }
-    return n;
-}
-
-// Exact e value of one logit.
-__device__ __forceinline__ float exact_e(const Ctx& c, const StreamSmem& sm, float l) {
-    const float x = c.unit ? l : xm_div_const(l, c.T, c.rT);
-    return xm::exp_f32(__fsub_rn(x, c.max_x), sm.exptab);
-}
-
-// Replays chunk t exactly starting from s (warp 0): kept values, or values
-// recomputed from the row.  A replayed chunk is one whose running sum crosses
-// a binade (often several, early in the row), so the 32 adds are done
-// serially -- redundantly in every lane -- rather than by the warp-parallel
-// chain, whose steps end at every crossing.
-__device__ float replay_chunk(StreamSmem& sm, const Ctx& c, int t, uint32_t side_plus1, float s) {
-    const int lane = threadIdx.x & 31;
-    const int base = t * kSC;
-    const int cnt = min(kSC, c.V - base);
-    if (side_plus1) {
-        const float* vals = sm.side[side_plus1 - 1];
-#pragma unroll 8
-        for (int i = 0; i < cnt; ++i) s = __fadd_rn(s, vals[i]);
-        return s;
-    }
-    const float e = (lane < cnt) ? exact_e(c, sm, __ldg(c.src + base + lane)) : 0.0f;
-    for (int i = 0; i < cnt; ++i) s = __fadd_rn(s, __shfl_sync(kFullMask, e, i));
-    return s;
-}
-
-// Exact serial softmax denominator from the chunk tables (warp 0).
-__device__ float resolve_S(StreamSmem& sm, const Ctx& c) {
-    const int lane = threadIdx.x & 31;
-    float s = 0.0f;
-    const int nseg = (c.nch + 31) / 32;
-    for (int seg = 0; seg < nseg; ++seg) {
-        const float4 wf = sm.wfn[seg];
-        const uint32_t wz = __float_as_uint(wf.z);
-        if (wz & kFClean) {
-            float s2 = s;
-            if (xm::chain_apply(s2, __float_as_uint(wf.w), xm::ChainFn{wf.x, wf.y, wz & 3u})) {
-                s = s2;
-                continue;
-            }
-        }
-        // chunk-level walk, picking per chunk the function of the current binade
-        const int cnt = min(32, c.nch - seg * 32);
-        const float4 ent = (lane < cnt) ? sm.fn[seg * 32 + lane] : make_float4(0, 0, 0, 0);
-        const uint32_t ez = __float_as_uint(ent.z);
-        float4 aent = make_float4(0, 0, 0, 0);
-        if (lane < cnt && (ez & kFAlt)) aent = sm.alt[(ez >> 8) & 0xFFu];
-        const uint32_t az = __float_as_uint(aent.z);
-        int cpos = 0;
-        while (cpos < cnt) {
-            if (regular_sum(s)) {
-                const uint32_t eb = xm::binade_of(s);
-                const bool use_p = (ez & kFClean) && __float_as_uint(ent.w) == eb;
-                const bool use_a = !use_p && (ez & kFAlt) && (az & kFClean) && __float_as_uint(aent.w) == eb;
-                const bool has = (lane >= cpos) && (lane < cnt) && (use_p || use_a);
-                xm::ChainFn f = xm::chain_identity();
-                if (has) f = use_p ? xm::ChainFn{ent.x, ent.y, ez & 3u} : xm::ChainFn{aent.x, aent.y, az & 3u};
-                const unsigned hm = __ballot_sync(kFullMask, has || lane < cpos);
-                const int fi = (~hm) ? (__ffs(~hm) - 1) : 32;
-                f = warp_incl_compose(f);
-                const float hi = __uint_as_float((eb + 1u) << 23);
-                const float L = (__float_as_uint(s) & 1u) ? f.L1 : f.L0;
-                const bool inb = (lane < cpos) || ((lane < fi) && (L <= __fsub_rn(hi, s)));
-                const unsigned inm = __ballot_sync(kFullMask, inb);
-                const int m = (~inm) ? (__ffs(~inm) - 1) : 32;  // chunks [cpos, m) resolve exactly
-                if (m > cpos) {
-                    s = __shfl_sync(kFullMask, __fadd_rn(s, L), m - 1);
-                    cpos = m;
-                }
-                if (cpos < cnt) {
-                    const uint32_t sp = __shfl_sync(kFullMask, ez >> 16, cpos);
-                    s = replay_chunk(sm, c, seg * 32 + cpos, sp, s);
-                    ++cpos;
-                }
-            } else {
-                const uint32_t sp = __shfl_sync(kFullMask, ez >> 16, cpos);
-                s = replay_chunk(sm, c, seg * 32 + cpos, sp, s);
-                ++cpos;
-            }
-        }
-    }
-    return s;
-}
-
-// ---------------------------------------------------------------------------
-// Large nuclei: the serial cumulative sum of the sorted p (llama2.c:1036-1054)
-// walked by chunk functions, as the softmax denominator is resolved.
-// ---------------------------------------------------------------------------
-
-// All threads: chunk t = sorted keys [32t, 32t + 32) of the first n0; its
-// incoming cumulative sum is guessed from a block scan of approximate chunk
-// sums.  Fills fn / alt / wfn (free again once S is resolved).
-__device__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int n0) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nchk = (n0 + kSC - 1) / kSC;
-    if (tid == 0) sm.n_alt = 0;
-    float sig[kStrips], gss[kStrips];
-#pragma unroll
-    for (int sidx = 0; sidx < kStrips; ++sidx) {
-        const int t = sidx * kST + tid;
-        float a = 0.0f;
-        if (t < nchk) {
-            const int cnt = min(kSC, n0 - kSC * t);
-            for (int j = 0; j < cnt; ++j) a += key_prob(kb[kSC * t + j]);
-        }
-        sig[sidx] = a;
-    }
-    float off = 0.0f;
-#pragma unroll
-    for (int sidx = 0; sidx < kStrips; ++sidx) {
-        const ScanF sc = block_scan_f(sig[sidx], sm);
-        gss[sidx] = off + sc.excl;
-        off += sc.total;
-    }
-#pragma unroll 1
-    for (int sidx = 0; sidx < kStrips; ++sidx) {
-        const int t = sidx * kST + tid;
-        const bool valid = t < nchk;
-        const int cnt = valid ? min(kSC, n0 - kSC * t) : 0;
-        uint32_t alt = 0u;
-        const uint32_t eb = valid ? xm::chain_guess_primary(gss[sidx], sig[sidx], alt) : 0u;
-        const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
-        const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
-        float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
-        for (int j = 0; j < cnt; ++j) {
-            const float x = key_prob(kb[kSC * t + j]);
-            v0 = __fadd_rn(v0, x);
-            v1 = __fadd_rn(v1, x);
-            w0 = __fadd_rn(w0, x);
-            w1 = __fadd_rn(w1, x);
-        }
-        const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
-        const bool aclean = valid && alt != 0u && (__float_as_uint(w0) >> 23) == alt && (__float_as_uint(w1) >> 23) == alt;
-        const xm::ChainFn f{__fsub_rn(v0, lo), __fsub_rn(v1, lo1),
-                            (__float_as_uint(v0) & 1u) | ((__float_as_uint(v1) & 1u) << 1)};
-        uint32_t z = (clean ? (f.pbits | kFClean) : 0u) | (valid ? kFValid : 0u);
-        if (aclean) {
-            const int ai = atomicAdd(&sm.n_alt, 1);
-            if (ai < kAltCap) {
-                sm.alt[ai] = make_float4(__fsub_rn(w0, alo), __fsub_rn(w1, alo1),
-                                         __uint_as_float((__float_as_uint(w0) & 1u) |
-                                                         ((__float_as_uint(w1) & 1u) << 1) | kFClean),
-                                         __uint_as_float(alt));
-                z |= kFAlt | ((uint32_t)ai << 8);
-            }
-        }
-        if (valid) sm.fn[t] = make_float4(f.L0, f.L1, __uint_as_float(z), __uint_as_float(eb));
-        const uint32_t eb0 = __shfl_sync(kFullMask, eb, 0);
-        const bool uni = __all_sync(kFullMask, !valid || (clean && eb == eb0 && !(z & kFAlt)));
-        const xm::ChainFn F = warp_incl_compose((valid && clean) ? f : xm::chain_identity());
-        if (lane == 31)
-            sm.wfn[sidx * kSW + warp] =
-                make_float4(F.L0, F.L1, __uint_as_float(F.pbits | (uni ? kFClean : 0u)), __uint_as_float(eb0));
-    }
-    __syncthreads();
-}
-
-// Warp 0: the first i < n with cum_i = fl(cum_{i-1} + p_i) > theta (cum is
-// then cum_i), or n (cum = cum_{n-1}), over the chunk functions of
-// build_walk_fns (built for n0 >= n keys).  Whole segments and chunks are
-// applied while they stay in one binade and end at or below theta; the chunk
-// that crosses theta or a binade is walked element by element.
-__device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, int n, float theta, float& cum) {
-    const int lane = threadIdx.x & 31;
-    float s = 0.0f;
-    const int nchk = (n + kSC - 1) / kSC;
-    const int nseg = (nchk + 31) / 32;
-    for (int seg = 0; seg < nseg; ++seg) {
-        const int cnt = min(32, nchk - seg * 32);
-        const float4 wf = sm.wfn[seg];
-        const uint32_t wz = __float_as_uint(wf.z);
-        // a whole segment only when all of its chunks are inside [0, n)
-        if ((wz & kFClean) && seg * 32 * kSC + 32 * kSC <= n) {
-            float s2 = s;
-            if (xm::chain_apply(s2, __float_as_uint(wf.w), xm::ChainFn{wf.x, wf.y, wz & 3u}) && !(s2 > theta)) {
-                s = s2;
-                continue;
-            }
-        }
-        // chunks wholly inside [0, n) may use their functions
-        const int t_lane = seg * 32 + lane;
-        const bool whole = (t_lane + 1) * kSC <= n;
-        const float4 ent = (lane < cnt) ? sm.fn[t_lane] : make_float4(0, 0, 0, 0);
-        const uint32_t ez = __float_as_uint(ent.z);
-        float4 aent = make_float4(0, 0, 0, 0);
-        if (lane < cnt && (ez & kFAlt)) aent = sm.alt[(ez >> 8) & 0xFFu];
-        const uint32_t az = __float_as_uint(aent.z);
-        int cpos = 0;
-        while (cpos < cnt) {
-            if (regular_sum(s)) {
-                const uint32_t eb = xm::binade_of(s);
-                const bool use_p = whole && (ez & kFClean) && __float_as_uint(ent.w) == eb;
-                const bool use_a = whole && !use_p && (ez & kFAlt) && (az & kFClean) && __float_as_uint(aent.w) == eb;
-                const bool has = (lane >= cpos) && (lane < cnt) && (use_p || use_a);
-                xm::ChainFn f = xm::chain_identity();
-                if (has) f = use_p ? xm::ChainFn{ent.x, ent.y, ez & 3u} : xm::ChainFn{aent.x, aent.y, az & 3u};
-                const unsigned hm = __ballot_sync(kFullMask, has || lane < cpos);
-                const int fi = (~hm) ? (__ffs(~hm) - 1) : 32;
-                f = warp_incl_compose(f);
-                const float hi = __uint_as_float((eb + 1u) << 23);
-                const float L = (__float_as_uint(s) & 1u) ? f.L1 : f.L0;
-                const bool fits_b = (lane < fi) && (L <= __fsub_rn(hi, s));
-                const float sl = __fadd_rn(s, L);
-                // chunks [cpos, m) end inside the binade and at or below theta
-                const bool inb = (lane < cpos) || (fits_b && !(sl > theta));
-                const unsigned inm = __ballot_sync(kFullMask, inb);
-                const int m = (~inm) ? (__ffs(~inm) - 1) : 32;
-                if (m > cpos) {
-                    s = __shfl_sync(kFullMask, sl, m - 1);
-                    cpos = m;
-                }
-            }
-            if (cpos < cnt) {
-                const int base = (seg * 32 + cpos) * kSC;
-                const int ne = min(kSC, n - base);
-                // the crossing chunk: 32 serial adds (one coalesced load, shuffles)
-                const float x = (lane < ne) ? key_prob(kb[base + lane]) : 0.0f;
-                for (int i = 0; i < ne; ++i) {
-                    s = __fadd_rn(s, __shfl_sync(kFullMask, x, i));
-                    if (s > theta) {
-                        cum = s;
-                        return base + i;
-                    }
-                }
-                ++cpos;
-            }
-        }
-    }
-    cum = s;
-    return n;
-}
-
-// Sorts every bin 0..D of the scattered nucleus by (e desc, index asc).  Warps
-// 1-7 take groups of 32 bins from a shared counter (warp 0 resolving S in the
-// meantime; having it join afterwards measured slower).  Bins of up to 16
-// keys: each key's rank is the number of
-// larger keys in its bin (keys are distinct); larger bins: bitonic networks.
-// Inside one bin (not the last) the value's top 15 bits are fixed, so 32-bit
-// keys (low 17 value bits, 0x7FFF - index) order them for V < 0x7FFF.
-__device__ void sort_bins(StreamSmem& sm, unsigned long long* kb, int D, int K, int V) {
-    const int lane = threadIdx.x & 31;
-    for (;;) {
-        int g = 0;
-        if (lane == 0) g = atomicAdd(&sm.sort_next, 1);
-        const int b0 = __shfl_sync(kFullMask, g, 0) * 32;
-        if (b0 > D) break;
-        const int b = b0 + lane;
-        int s0 = 0, n = 0;
-        if (b <= D) {
-            s0 = sm.bstart[b];
-            n = sm.hist[b] - s0;
-            if (s0 < 0 || s0 + n > K || n > 256) sm.flag = 1;
-        }
-        unsigned todo = __ballot_sync(kFullMask, n >= 2 && n <= 256 && s0 >= 0 && s0 + n <= K);
-        const unsigned small = __ballot_sync(kFullMask, n <= 16);
-        while (todo) {
-            const int src = __ffs(todo) - 1;
-            todo &= todo - 1;
-            const int ss = __shfl_sync(kFullMask, s0, src);
-            const int nn = __shfl_sync(kFullMask, n, src);
-            unsigned long long* seg = kb + ss;
-            const bool narrow = (b0 + src < kBins - 1) && V < 0x7FFF;
-            if (nn <= 16) {
-                // two small bins at a time, one per half-warp
-                const unsigned rest = todo & small;
-                const int src2 = rest ? (__ffs(rest) - 1) : -1;
-                if (src2 >= 0) todo &= ~(1u << src2);
-                const int ss2 = __shfl_sync(kFullMask, s0, src2 < 0 ? 0 : src2);
-                const int nn2 = (src2 < 0) ? 0 : __shfl_sync(kFullMask, n, src2 < 0 ? 0 : src2);
-                const bool narrow2 = narrow && (src2 < 0 || b0 + src2 < kBins - 1);
-                const int hl = lane & 15;
-                const int my_ss = (lane < 16) ? ss : ss2;
-                const int my_nn = (lane < 16) ? nn : nn2;
-                const unsigned long long key = (hl < my_nn) ? kb[my_ss + hl] : 0ull;
-                const int top = max(nn, nn2);
-                int rank = 0;
-                if (narrow2) {
-                    const uint32_t vb = (uint32_t)(key >> 32);
-                    const uint32_t k32 = ((vb & 0x1FFFFu) << 15) | (uint32_t)(0x7FFF - key_index(key));
-                    for (int t = 0; t < top; ++t) {
-                        const uint32_t o = __shfl_sync(kFullMask, k32, (lane & 16) | t);
-                        rank += (t < my_nn && o > k32) ? 1 : 0;
-                    }
-                } else {
-                    for (int t = 0; t < top; ++t) {
-                        const unsigned long long o = __shfl_sync(kFullMask, key, (lane & 16) | t);
-                        rank += (t < my_nn && o > key) ? 1 : 0;
-                    }
-                }
-                __syncwarp();
-                if (hl < my_nn) kb[my_ss + rank] = key;
-                __syncwarp();
-            } else if (narrow) {
-                if (nn <= 32) warp_sort_bin<1>(seg, nn, lane);
-                else if (nn <= 64) warp_sort_bin<2>(seg, nn, lane);
-                else if (nn <= 128) warp_sort_bin<4>(seg, nn, lane);
-                else warp_sort_bin<8>(seg, nn, lane);
-            } else {
-                if (nn <= 32) warp_sort_desc<1>(seg, nn, lane);
-                else if (nn <= 64) warp_sort_desc<2>(seg, nn, lane);
-                else if (nn <= 128) warp_sort_desc<4>(seg, nn, lane);
-                else warp_sort_desc<8>(seg, nn, lane);
-            }
-        }
-    }
-}
-
-__device__ void defer_row_s(const RowLaunch& p, int row) {
-    const int k = atomicAdd(p.defer_count, 1);
-    p.defer_rows[k] = row;
-}
-
-__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
-
-// Loads chunk t (32 floats) with eight independent 16-byte loads.
-__device__ __forceinline__ void load_chunk(const Ctx& c, int t, float (&a)[kSC]) {
-    const int base = t * kSC;
-    const int cnt = min(kSC, c.V - base);  // multiple of 4 when > 0
-#pragma unroll
-    for (int g = 0; g < kSC / 4; ++g) {
-        float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (4 * g < cnt) q = ldg4(c.src + base + 4 * g);
-        a[4 * g] = q.x;
-        a[4 * g + 1] = q.y;
-        a[4 * g + 2] = q.z;
-        a[4 * g + 3] = q.w;
-    }
-}
-
-
-// x = l/T for the rows the kernel takes (see the lean-row rule in the kernel).
-__device__ __forceinline__ float div_lean(float l, const Ctx& c) {
-    const float q = __fmul_rn(l, c.rT);
-    const float r = __fmaf_rn(-q, c.T, l);
-    return __fmaf_rn(r, c.rT, q);
-}
-
-// Pass 2 over one chunk: exact e = exp(l/T - max) of every element (a
-// per-element skip of the values the serial sum absorbs costs more in
-// divergence than the exp it saves), the chain sums in the primary (v0, v1)
-// and alternative (w0, w1) binade, candidate counts in the histogram, and the
-// values of kept chunks.  kGeneral: a partial chunk, or a row whose d range
-// reaches below the fast exp range.
-template <bool kGeneral>
-__device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx& c, StreamSmem& sm, float e_min,
-                                            float* keep, float& v0, float& v1, float& w0, float& w1) {
-    // three granules in flight: rotate qa <- qb <- qc <- load(g + 3)
-    float4 qa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), qb = qa, qc = qa;
-    if (!kGeneral || 0 < cnt) qa = ldg4(cp);
-    if (!kGeneral || 4 < cnt) qb = ldg4(cp + 4);
-    if (!kGeneral || 8 < cnt) qc = ldg4(cp + 8);
-#pragma unroll 1
-    for (int g = 0; g < kSC / 4; ++g) {
-        float4 qn = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (4 * (g + 3) < (kGeneral ? cnt : kSC)) qn = ldg4(cp + 4 * (g + 3));
-        float a[4] = {qa.x, qa.y, qa.z, qa.w};
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            float e = 0.0f;
-            if (!kGeneral || 4 * g + w < cnt) {
-                const float d = __fsub_rn(div_lean(a[w], c), c.max_x);
-                e = kGeneral ? xm::exp_f32(d, sm.exptab) : xm::exp_normal_range(d, sm.exptab);
-                if (e >= e_min) atomicAdd(&sm.hist[bin_of(e)], 1);
-            }
-            a[w] = e;
-            v0 = __fadd_rn(v0, e);
-            v1 = __fadd_rn(v1, e);
-            w0 = __fadd_rn(w0, e);
-            w1 = __fadd_rn(w1, e);
-        }
-        if (keep) reinterpret_cast<float4*>(keep)[g] = make_float4(a[0], a[1], a[2], a[3]);
-        qa = qb;
-        qb = qc;
-        qc = qn;
-    }
-}
-
-__global__ void __launch_bounds__(kST, 4) row_stream_kernel(RowLaunch p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    StreamSmem& sm = *reinterpret_cast<StreamSmem*>(smem_raw);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid < xm::kExpTableSize) sm.exptab[tid] = xm::exp_table_entry(tid);
-    __syncthreads();
-    const int V = p.vocab;
-    const int nch = (V + kSC - 1) / kSC;
-    // per-CTA L2-resident scratch for nuclei above the on-chip capacity
-    unsigned long long* super = p.workspace + (long long)blockIdx.x * p.ws_stride;
-
-    for (int row = blockIdx.x; row < p.batch; row += gridDim.x) {
-        Ctx c;
-        c.src = p.logits + (long long)row * p.ld;
-        c.V = V;
-        c.nch = nch;
-        c.T = p.temperature_rows ? p.temperature_rows[row] : p.temperature;
-        const float topp = p.topp_rows ? p.topp_rows[row] : p.topp;
-        const bool greedy = (c.T == 0.0f);
-        if (!greedy && (topp <= 0.0f || topp >= 1.0f)) {  // sample_mult rows: general kernel
-            if (tid == 0) defer_row_s(p, row);
-            continue;
-        }
-
-        if (greedy) {
-            // first index of the strict max, NaN at index 0 wins (llama2.c:981-992)
-            float bv = -INFINITY;
-            int bi = 0x7FFFFFFF;
-            for (int sidx = 0; sidx < kStrips; ++sidx) {
-                const int t = sidx * kST + tid;
-                if (t >= nch) break;
-                float a[kSC];
-                load_chunk(c, t, a);
-                const int cnt = min(kSC, V - t * kSC);
-#pragma unroll
-                for (int j = 0; j < kSC; ++j)
-                    if (j < cnt && (a[j] > bv || (a[j] == bv && t * kSC + j < bi))) {
-                        bv = a[j];
-                        bi = t * kSC + j;
-                    }
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                const float ov = __shfl_xor_sync(kFullMask, bv, o);
-                const int oi = __shfl_xor_sync(kFullMask, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            if (lane == 0) {
-                sm.red_a[warp] = bv;
-                sm.red_i[warp] = bi;
-            }
-            __syncthreads();
-            if (tid == 0) {
-                for (int w = 1; w < kSW; ++w)
-                    if (sm.red_a[w] > bv || (sm.red_a[w] == bv && sm.red_i[w] < bi)) {
-                        bv = sm.red_a[w];
-                        bi = sm.red_i[w];
-                    }
-                p.out_ids[row] = (isnan(__ldg(c.src)) || bi == 0x7FFFFFFF) ? 0 : bi;
-                if (p.row_flags) p.row_flags[row] = 0;
-            }
-            __syncthreads();
-            continue;
-        }
-
-        // ---- pass 1: max/min of l; per-chunk approximate sum of exp(x - max)
-        c.rT = __frcp_rn(c.T);
-        c.unit = (c.T == 1.0f);
-        const float k2 = c.rT * 1.4426950408889634f;  // log2(e)/T, approximate scale
-        float mxl = -INFINITY, mnl = INFINITY, M2loc = -3.4e38f;
-        float cm2[kStrips], cs2[kStrips];
-        const float4* stats = p.stats ? p.stats + (long long)row * p.stats_ld : nullptr;
-#pragma unroll
-        for (int sidx = 0; sidx < kStrips; ++sidx) {
-            const int t = sidx * kST + tid;
-            float m2 = -3.4e38f, s2 = 0.0f;
-            if (stats) {
-                // the same quantities from the classifier GEMM epilogue
-                if (t < nch) {
-                    const float4 q = stats[t];
-                    mxl = fmaxf(mxl, q.x);
-                    mnl = fminf(mnl, q.y);
-                    m2 = fmaxf(m2, (k2 > 0.0f ? q.x : q.y) * k2);
-                    s2 = q.z;
-                }
-            } else if (t < nch) {
-                float a[kSC];
-                load_chunk(c, t, a);  // eight loads in flight
-                const int cnt = min(kSC, V - t * kSC);
-                if (cnt == kSC) {
-#pragma unroll
-                    for (int j = 0; j < kSC; ++j) {
-                        mxl = fmaxf(mxl, a[j]);
-                        mnl = fminf(mnl, a[j]);
-                        m2 = fmaxf(m2, a[j] * k2);
-                    }
-#pragma unroll
-                    for (int j = 0; j < kSC; ++j) s2 += ex2_approx(__fmaf_rn(a[j], k2, -m2));
-                } else {
-#pragma unroll
-                    for (int j = 0; j < kSC; ++j)
-                        if (j < cnt) {
-                            mxl = fmaxf(mxl, a[j]);
-                            mnl = fminf(mnl, a[j]);
-                            m2 = fmaxf(m2, a[j] * k2);
-                        }
-#pragma unroll
-                    for (int j = 0; j < kSC; ++j)
-                        if (j < cnt) s2 += ex2_approx(__fmaf_rn(a[j], k2, -m2));
-                }
-            }
-            cm2[sidx] = m2;
-            cs2[sidx] = s2;
-            M2loc = fmaxf(M2loc, m2);
-        }
-        float wmx = mxl, wmn = mnl, wm2 = M2loc;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            wmx = fmaxf(wmx, __shfl_xor_sync(kFullMask, wmx, o));
-            wmn = fminf(wmn, __shfl_xor_sync(kFullMask, wmn, o));
-            wm2 = fmaxf(wm2, __shfl_xor_sync(kFullMask, wm2, o));
-        }
-        if (lane == 0) {
-            sm.red_a[warp] = wmx;
-            sm.red_b[warp] = wmn;
-            sm.red_c[warp] = wm2;
-        }
-        if (tid == 0) {
-            sm.n_alt = 0;
-            sm.n_side = 0;
-            sm.flag = 0;
-            sm.dbin = -1;
-            sm.sort_next = 0;
-        }
-        for (int b = tid; b < kBins; b += kST) sm.hist[b] = 0;
-        __syncthreads();
-        float MX = -INFINITY, MN = INFINITY, M2 = -3.4e38f;
-#pragma unroll
-        for (int w = 0; w < kSW; ++w) {
-            MX = fmaxf(MX, sm.red_a[w]);
-            MN = fminf(MN, sm.red_b[w]);
-            M2 = fmaxf(M2, sm.red_c[w]);
-        }
-        __syncthreads();  // red_* are reused by the scans below
-        c.max_x = c.unit ? MX : (c.T > 0.0f ? __fdiv_rn(MX, c.T) : __fdiv_rn(MN, c.T));
-        // Rows this kernel takes: x = l/T by the unguarded Markstein division,
-        // correctly rounded for |T| in [2^-10, 2^10] and |l| in [2^-60, 2^60]
-        // (and for l = 0).  A nonzero |l| < 2^-60 gives |x| < 2^-49, below
-        // half an ulp of max_x when |max_x| >= 2^-24, so d = fl(x - max_x) =
-        // -max_x whatever the quotient's last bits.  Other rows (huge logits,
-        // extreme temperatures, a tiny row maximum) go to the general kernel.
-        {
-            const float aT = fabsf(c.T);
-            const bool lean = aT >= 0x1p-10f && aT <= 0x1p10f && fmaxf(fabsf(MX), fabsf(MN)) <= 0x1p60f &&
-                              fabsf(c.max_x) >= 0x1p-24f;
-            if (!lean) {
-                if (tid == 0) defer_row_s(p, row);
-                continue;
-            }
-        }
-        // approximate chunk sums in units of exp(x - max); exclusive prefix in
-        // chunk order (strip-major)
-        float sig[kStrips], gss[kStrips];
-        float strip_off = 0.0f;
-#pragma unroll
-        for (int sidx = 0; sidx < kStrips; ++sidx) {
-            sig[sidx] = cs2[sidx] * ex2_approx(cm2[sidx] - M2);
-            const ScanF sc = block_scan_f(sig[sidx], sm);
-            gss[sidx] = strip_off + sc.excl;
-            strip_off += sc.total;
-        }
-        const float s_approx = strip_off;
-
-        // ---- pass 2: exact e where it matters, chunk functions, histogram
-        const float cutoff = __fdiv_rn(__fsub_rn(1.0f, topp), (float)(V - 1));  // llama2.c:1024
-        const float e_min = cutoff * s_approx * 0.9921875f;
-        const float d_cand = (e_min > 0.0f) ? __logf(e_min) - 1e-3f : -INFINITY;
-        // every d = fl(x - max) lies in [fl(min_x - max_x), 0]: rows whose
-        // range stays inside the fast exp range skip the range check
-        const float min_x = c.unit ? MN : (c.T > 0.0f ? __fdiv_rn(MN, c.T) : __fdiv_rn(MX, c.T));
-        const bool wide = !(__fsub_rn(min_x, c.max_x) >= xm::kExpFastMin);
-        // a NaN logit makes the approximate sum NaN (ex2.approx(NaN) = NaN),
-        // and the reference's softmax then yields all-NaN probabilities: such
-        // rows skip pass 2 (whose fast exp does not carry NaN through)
-        const bool nan_row = isnan(s_approx);
-        bool nan_any = false;
-#pragma unroll 1
-        for (int sidx = 0; sidx < (nan_row ? 0 : kStrips); ++sidx) {
-            const int t = sidx * kST + tid;
-            const bool valid = t < nch;
-            const int cnt = valid ? min(kSC, V - t * kSC) : 0;
-            uint32_t alt = 0u;
-            const uint32_t eb = valid ? xm::chain_guess_primary(gss[sidx], sig[sidx], alt) : 0u;
-            // chunks whose binade is unknown or near a boundary keep their
-            // values for a possible serial replay
-            float* keep = nullptr;
-            int keep_idx = -1;
-            if (valid && (eb == 0u || alt != 0u)) {
-                keep_idx = atomicAdd(&sm.n_side, 1);
-                if (keep_idx < kSideCap) keep = sm.side[keep_idx];
-                else keep_idx = -1;
-            }
-            const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
-            const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
-            float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
-            const float* cp = c.src + t * kSC;
-            if (cnt == kSC && !wide)
-                pass2_chunk<false>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
-            else if (valid)
-                pass2_chunk<true>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
-            nan_any |= isnan(v0);
-            // chunk functions (primary and alternative binade)
-            const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
-            const bool aclean = valid && alt != 0u && (__float_as_uint(w0) >> 23) == alt && (__float_as_uint(w1) >> 23) == alt;
-            const xm::ChainFn f{__fsub_rn(v0, lo), __fsub_rn(v1, lo1),
-                                (__float_as_uint(v0) & 1u) | ((__float_as_uint(v1) & 1u) << 1)};
-            uint32_t z = (clean ? (f.pbits | kFClean) : 0u) | (valid ? kFValid : 0u);
-            if (aclean) {
-                const int ai = atomicAdd(&sm.n_alt, 1);
-                if (ai < kAltCap) {
-                    sm.alt[ai] = make_float4(__fsub_rn(w0, alo), __fsub_rn(w1, alo1),
-                                             __uint_as_float((__float_as_uint(w0) & 1u) |
-                                                             ((__float_as_uint(w1) & 1u) << 1) | kFClean),
-                                             __uint_as_float(alt));
-                    z |= kFAlt | ((uint32_t)ai << 8);
-                }
-            }
-            if (keep_idx >= 0) z |= (uint32_t)(keep_idx + 1) << 16;
-            if (valid) sm.fn[t] = make_float4(f.L0, f.L1, __uint_as_float(z), __uint_as_float(eb));
-            // segment (= warp within the strip) function when all chunks are
-            // clean in one binade
-            const uint32_t eb0 = __shfl_sync(kFullMask, eb, 0);
-            const bool uni = __all_sync(kFullMask, !valid || (clean && eb == eb0 && !(z & kFAlt)));
-            const xm::ChainFn F = warp_incl_compose((valid && clean) ? f : xm::chain_identity());
-            if (lane == 31)
-                sm.wfn[sidx * kSW + warp] =
-                    make_float4(F.L0, F.L1, __uint_as_float(F.pbits | (uni ? kFClean : 0u)), __uint_as_float(eb0));
-        }
-        const bool row_nan = (__syncthreads_or(nan_any) != 0) || nan_row;
-
-        // ---- coin (drawn before the walk, llama2.c:1094); state committed at the end
-        unsigned long long st = 0;
-        float coin = 0.0f;
-        if (p.coins) {
-            coin = p.coins[row];
-        } else {
-            st = p.rng_state[row];
-            coin = draw_coin(st);
-        }
-        int flags = 0, id = 0;
-        bool defer = false;
-        if (row_nan) {
-            flags = kFlagNan | kFlagNoCand;
-        } else {
-            // ---- nucleus bins from the histogram: guaranteed mass of bins 0..D
-            // against topp plus the fp32 drift bound, with the approximate S
-            // scaled up by the 2^-7 margin that bounds its distance to the
-            // exact serial S (checked after the walk: a miss defers the row)
-            int h[kBinsPerThread];
-            int hc = 0;
-            float hm = 0.0f;
-#pragma unroll
-            for (int q = 0; q < kBinsPerThread; ++q) {
-                const int b = tid * kBinsPerThread + q;
-                h[q] = sm.hist[b];
-                hc += h[q];
-                hm += (float)h[q] * bin_lo(b);
-            }
-            const ScanF ms = block_scan_f(hm, sm);
-            int ctot;
-            const int cex = block_scan_i(hc, sm, ctot) - hc;
-            const float target = (topp + 4096.0f * 0x1p-24f + 1e-5f) * s_approx * 1.0078125f;
-            if (ms.incl >= target && ms.excl < target) {
-                float m = ms.excl;
-                int cc = cex, d = tid * kBinsPerThread + kBinsPerThread - 1;
-#pragma unroll
-                for (int q = 0; q < kBinsPerThread; ++q) {
-                    cc += h[q];
-                    m += (float)h[q] * bin_lo(tid * kBinsPerThread + q);
-                    if (m >= target) {
-                        d = tid * kBinsPerThread + q;
-                        break;
-                    }
-                }
-                sm.dbin = d;
-                sm.ksel = cc;
-            }
-            __syncthreads();
-            int D = sm.dbin, K = sm.ksel;
-            const bool all_cand = D < 0;
-            if (all_cand) {
-                D = kBins - 1;
-                K = ctot;
-            }
-            // the nucleus lives on chip, or in the CTA's L2 scratch
-            unsigned long long* kb = (K <= kKCap) ? sm.kbuf : super;
-            // the L2 scratch holds any nucleus (ws_stride >= V + 4096 keys)
-            const bool fits = K <= p.ws_stride;
-            if (fits) {
-                // bin offsets (hist becomes the scatter cursor)
-                int run = cex;
-#pragma unroll
-                for (int q = 0; q < kBinsPerThread; ++q) {
-                    const int b = tid * kBinsPerThread + q;
-                    if (b <= D) {
-                        sm.bstart[b] = (unsigned short)run;
-                        sm.hist[b] = run;
-                        run += h[q];
-                    }
-                }
-            }
-            __syncthreads();
-            if (warp == 0) {
-                // ---- exact S (overlaps the extraction below)
-                const float S = resolve_S(sm, c);
-                if (lane == 0) sm.fval = S;
-            } else if (fits) {
-                // ---- re-read the row (L2) and place the elements of bins
-                // 0..D, then sort each bin by (e desc, index asc)
-                // Logit-space pre-filter: every element of bins 0..D has
-                // e >= e_x = max(lower edge of bin D, e_min), so d >= ln(e_x) -
-                // eps; d = fl(fl(l/T) - max) is monotone in l, and l beyond
-                // l_lo (T > 0: below; T < 0: above) by a relative 2^-20 plus
-                // the absolute 1e-3 margin cannot be one of them.
-                const float e_x = fmaxf(bin_lo(D), e_min);
-                const float d_x = (e_x > 0.0f) ? __logf(e_x) - 1e-3f : -INFINITY;
-                const float tl = __fmul_rn(c.T, __fadd_rn(c.max_x, d_x));
-                const float l_lo = (c.T > 0.0f) ? (tl - fabsf(tl) * 0x1p-20f - fabsf(c.T) * 5e-4f)
-                                                : (tl + fabsf(tl) * 0x1p-20f + fabsf(c.T) * 5e-4f);
-                const float sg = (c.T > 0.0f) ? 1.0f : -1.0f;
-                const float l_cmp = sg * l_lo;
-                const int u = tid - 32, nu = kST - 32;
-                const float4* row4 = reinterpret_cast<const float4*>(c.src);
-                const int ng = V / 4;
-                for (int g0 = u; g0 < ng; g0 += 4 * nu) {
-                    float4 q[4];
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        q[k] = (g0 + k * nu < ng) ? __ldg(row4 + g0 + k * nu)
-                                                  : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-                    uint32_t m = 0u;
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        m |= (sg * q[k].x < l_cmp) ? 0u : (1u << (4 * k));
-                        m |= (sg * q[k].y < l_cmp) ? 0u : (2u << (4 * k));
-                        m |= (sg * q[k].z < l_cmp) ? 0u : (4u << (4 * k));
-                        m |= (sg * q[k].w < l_cmp) ? 0u : (8u << (4 * k));
-                    }
-                    // padding (-inf * sg) never passes for T > 0; for T < 0 it
-                    // is excluded by the granule bound below
-                    while (m) {
-                        const int j = __ffs(m) - 1;
-                        m &= m - 1;
-                        const int gi = g0 + (j >> 2) * nu;
-                        if (gi >= ng) continue;
-                        const int idx = 4 * gi + (j & 3);
-                        const float d = __fsub_rn(div_lean(__ldg(c.src + idx), c), c.max_x);
-                        if (d >= d_cand) {
-                            const float e = xm::exp_f32(d, sm.exptab);
-                            if (e >= e_min) {
-                                const int b = bin_of(e);
-                                if (b <= D) {
-                                    const int pos = atomicAdd(&sm.hist[b], 1);
-                                    if (pos < K) kb[pos] = cand_key(e, idx);
-                                }
-                            }
-                        }
-                    }
-                }
-                named_bar(1, kST - 32);
-                sort_bins(sm, kb, D, K, V);
-            }
-            __syncthreads();
-            const float S = sm.fval;
-            if (!fits || sm.flag) {
-                defer = true;
-            } else {
-                // p = fl(e/S) in place of e (Markstein division: correctly
-                // rounded for S in [1, 2^15] and e >= 2^-60).  The same pass
-                // finds the end of the candidates proper (p >= cutoff form a
-                // prefix) from each key's successor, and whether any equal-p
-                // run exists.  Four keys per thread in flight.
-                const float rS = __frcp_rn(S);
-                auto to_p = [&](float e) {
-                    const float q = __fmul_rn(e, rS);
-                    return __fmaf_rn(__fmaf_rn(-q, S, e), rS, q);
-                };
-                if (tid == 0) {
-                    sm.n0 = 0;
-                    sm.n_pairs = 0;
-                }
-                __syncthreads();
-                for (int base = 0; base < K; base += 4 * kST) {  // uniform trip count (barrier inside)
-                    const int i0 = base + tid;
-                    unsigned long long k[4], kn[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int i = i0 + u * kST;
-                        k[u] = (i < K) ? kb[i] : 0ull;
-                        kn[u] = (i + 1 < K) ? kb[i + 1] : 0ull;
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int i = i0 + u * kST;
-                        if (i < K) {
-                            const float pv = to_p(key_prob(k[u]));
-                            const bool has_next = i + 1 < K;
-                            const float pn = has_next ? to_p(key_prob(kn[u])) : -1.0f;
-                            if (pn == pv) {
-                                const int q = atomicAdd(&sm.n_pairs, 1);
-                                if (q < kPairCap) sm.pairs[q] = i;
-                            }
-                            if (pv >= cutoff && !(pn >= cutoff)) sm.n0 = i + 1;
-                            k[u] = ((unsigned long long)__float_as_uint(pv) << 32) | (k[u] & 0xFFFFFFFFull);
-                        }
-                    }
-                    __syncthreads();  // every key of this round read before any is rewritten
-#pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        if (i0 + u * kST < K) kb[i0 + u * kST] = k[u];
-                }
-                // equal-p runs (sorted by e, so contiguous) go to index order,
-                // glibc qsort's order for ties; runs are a few keys, found from
-                // the recorded neighbour pairs (all positions if too many)
-                __syncthreads();
-                const int npairs = sm.n_pairs;
-                if (npairs > 0) {
-                    const bool listed = npairs <= kPairCap;
-                    const int nscan = listed ? npairs : K - 1;
-                    for (int q = tid; q < nscan; q += kST) {
-                        const int i = listed ? sm.pairs[q] : q;
-                        const unsigned long long a = kb[i];
-                        if ((a >> 32) == (kb[i + 1] >> 32) && (i == 0 || (kb[i - 1] >> 32) != (a >> 32))) {
-                            int j = i + 1;
-                            while (j < K && (kb[j] >> 32) == (a >> 32)) ++j;
-                            for (int x = i + 1; x < j; ++x) {  // insertion sort by index
-                                const unsigned long long kx = kb[x];
-                                int y = x - 1;
-                                while (y >= i && key_index(kb[y]) > key_index(kx)) {
-                                    kb[y + 1] = kb[y];
-                                    --y;
-                                }
-                                kb[y + 1] = kx;
-                            }
-                        }
-                    }
-                    __syncthreads();
-                }
-                const int n0 = sm.n0;
-                const bool big = n0 > kWalkDirect;
-                if (big) build_walk_fns(sm, kb, n0);  // all threads
-                if (warp == 0) {
-                    int res = -1;
-                    if (n0 == 0) {
-                        res = all_cand ? -2 : -1;
-                    } else {
-                        auto get = [&](int i) { return key_prob(kb[i]); };
-                        float cum = 0.0f;
-                        // llama2.c:1036-1043
-                        int last = big ? walk_chunks(sm, kb, n0, topp, cum) : warp_chain(get, n0, cum, topp);
-                        if (last >= n0) last = all_cand ? n0 - 1 : -1;  // llama2.c:1037
-                        if (last >= 0) {
-                            const float r = __fmul_rn(coin, cum);  // llama2.c:1046
-                            float s3 = 0.0f;
-                            int k = big ? walk_chunks(sm, kb, last + 1, r, s3) : warp_chain(get, last + 1, s3, r);
-                            if (k > last) k = last;  // llama2.c:1055
-                            res = key_index(kb[k]);
-                        }
-                    }
-                    if (lane == 0) sm.result = res;
-                }
-                __syncthreads();
-                const int res = sm.result;
-                if (res == -1) {
-                    defer = true;
-                } else if (res == -2) {
-                    flags |= kFlagNoCand;
-                    id = 0;
-                } else {
-                    id = res;
-                }
-            }
-        }
-        if (tid == 0) {
-            if (defer) {
-                defer_row_s(p, row);
-            } else {
-                p.out_ids[row] = id;
-                if (p.row_flags) p.row_flags[row] = flags;
-                if (!p.coins) p.rng_state[row] = st;
-            }
-        }
-        __syncthreads();
-    }
-}
-
-}  // namespace
-
-size_t stream_smem_bytes() { return sizeof(StreamSmem); }
+size_t stream_smem_bytes() { return rs256::smem_bytes() > rs1024::smem_bytes() ? rs256::smem_bytes() : rs1024::smem_bytes(); }
 int stream_ctas_per_sm() { return 4; }
 
-int launch_row_stream(const RowLaunch& p, int num_ctas, cudaStream_t stream) {
-    static std::atomic<unsigned long long> attr_done{0};
-    int dev = 0;
-    cudaError_t e0 = cudaGetDevice(&dev);
-    if (e0 != cudaSuccess) return -(int)e0;
-    const unsigned long long bit = 1ull << (dev & 63);
-    if (!(attr_done.load() & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(row_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)sizeof(StreamSmem));
-        if (e != cudaSuccess) return -(int)e;
-        attr_done.fetch_or(bit);
-    }
-    row_stream_kernel<<<num_ctas, kST, sizeof(StreamSmem), stream>>>(p);
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? 1 : -(int)e;
+int launch_row_stream(const RowLaunch& p, int num_sms, cudaStream_t stream) {
+    if (p.batch <= num_sms) return rs1024::launch(p, p.batch, stream);
+    const int ctas = p.batch < 4 * num_sms ? p.batch : 4 * num_sms;
+    return rs256::launch(p, ctas, stream);
 }
 
 }  // namespace b2s

@@ -237,7 +237,7 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
         q.ws_stride = (long long)stream_stride(V);
         q.stats = stats;
         q.stats_ld = stats_ld;
-        const int n = b2s::launch_row_stream(q, stream_ctas(c, batch), stream);
+        const int n = b2s::launch_row_stream(q, c->num_sms, stream);
         if (n < 0) return fail(SAMPLER_E_CUDA, "stream launch: %s", cudaGetErrorString((cudaError_t)(-n)));
         launches += n + 1;
         p.row_list = defer_rows;

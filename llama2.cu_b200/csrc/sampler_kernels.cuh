@@ -78,9 +78,10 @@ size_t row_kernel_smem_bytes();
 size_t stream_smem_bytes();
 int stream_ctas_per_sm();
 // The streaming kernel over all rows (greedy and top-p rows finish there;
-// the rest go to the deferred list).  workspace: ws_stride >= vocab u64
-// entries per CTA.
-int launch_row_stream(const RowLaunch& p, int num_ctas, cudaStream_t stream);
+// the rest go to the deferred list); it launches at most
+// stream_ctas_per_sm() * num_sms CTAs, each with ws_stride >= vocab u64
+// workspace entries.
+int launch_row_stream(const RowLaunch& p, int num_sms, cudaStream_t stream);
 // Persistent tcgen05 GEMM, one CTA per SM (at most num_sms CTAs).
 int launch_classifier_gemm(const GemmLaunch& p, int num_sms, cudaStream_t stream);
 // The same GEMM by CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles).
