@@ -165,7 +165,10 @@ const char* sampler_last_error(void);
  *   wcls       bf16 [vocab_size, dim] row-major (16-byte aligned)
  *   cfg        vocab_size % 32 == 0, <= SAMPLER_MAX_VOCAB; flags must be 0
  *   logits_out fp32 [batch, vocab_size] or NULL (then library-managed)
- * Other arguments as in sampler_batched().  Asynchronous on `stream`. */
+ * Other arguments as in sampler_batched().  Asynchronous on `stream`.
+ * The per-chunk statistics (and the logits when logits_out is NULL) live in
+ * buffers the library keeps per device, so fused calls that may overlap on
+ * one GPU (different streams or threads) must be serialized. */
 int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, const void* wcls, int batch,
                             int dim, const float* temperature_rows, const float* topp_rows, const float* coins,
                             unsigned long long* rng_state, int* out_ids, float* logits_out, int* row_flags,

@@ -33,7 +33,6 @@ struct StreamSmem {
     float red_a[kSW];
     float red_b[kSW];
     float red_c[kSW];
-    float red_s[kStrips][kSW];
     int red_i[kSW];
     int n_alt;
     int n_side;
