@@ -673,12 +673,17 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 load_chunk(c, t, a);  // eight loads in flight
                 const int cnt = min(kSC, V - t * kSC);
                 if (cnt == kSC) {
+                    // max of fl(a*k2) is fl(max(a)*k2) for k2 > 0 (rounding is
+                    // monotone), fl(min(a)*k2) for k2 < 0
+                    float cmx = -INFINITY, cmn = INFINITY;
 #pragma unroll
                     for (int j = 0; j < kSC; ++j) {
-                        mxl = fmaxf(mxl, a[j]);
-                        mnl = fminf(mnl, a[j]);
-                        m2 = fmaxf(m2, a[j] * k2);
+                        cmx = fmaxf(cmx, a[j]);
+                        cmn = fminf(cmn, a[j]);
                     }
+                    mxl = fmaxf(mxl, cmx);
+                    mnl = fminf(mnl, cmn);
+                    m2 = fmaxf(m2, (k2 > 0.0f ? cmx : cmn) * k2);
 #pragma unroll
                     for (int j = 0; j < kSC; ++j) s2 += ex2_approx(__fmaf_rn(a[j], k2, -m2));
                 } else {
