@@ -21,9 +21,9 @@
 //   warps 4-7  epilogue: tcgen05.ld of 32 columns at a time (one row per
 //              thread), fp32 logits to HBM and, per 32-column chunk, the
 //              statistics (max, min, approximate sum of exp((l - max)/T))
-// No cluster, no multicast: every CTA loads its own tiles (the kernel also
-// runs on every GPU of a multi-GPU job).  Every mbarrier wait is bounded; a
-// timeout sets the error word and drains the pipeline.
+// Every CTA loads its own tiles from this GPU's memory with plain TMA loads
+// (the kernels also run on every GPU of a multi-GPU job).  Every mbarrier
+// wait is bounded; a timeout sets the error word and drains the pipeline.
 #include "device_common.cuh"
 #include "sampler_kernels.cuh"
 
@@ -329,7 +329,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
 // and 128 rows of W per K step (32 KB, half the single-CTA ring's bytes per
 // FLOP) and holds the 128 x 256 fp32 accumulator of its rows in its own TMEM,
 // double-buffered.  The even CTA issues the MMAs.  Both CTAs' TMA loads
-// (.cta_group::2, no multicast) complete on the even CTA's stage barrier; the
+// (.cta_group::2, each into its own CTA's memory) complete on the even CTA's
+// stage barrier; the
 // even CTA's commits release the stage and hand over the accumulator in both
 // CTAs (one commit per CTA, to that CTA's barrier), and every epilogue warp
 // of the pair arrives on the even CTA's accumulator-free barrier.
