@@ -341,7 +341,7 @@ constexpr int kPHalf = 128;           // rows of each operand staged per CTA
 constexpr int kPStages = 6;
 constexpr int kPABytes = kPHalf * kGK * 2;  // 16 KB
 constexpr int kPBBytes = kPHalf * kGK * 2;  // 16 KB
-constexpr int kPGroupM = 8;           // pair M blocks swept together
+constexpr int kPGroupM = 16;          // pair M blocks swept together (L2 reuse of W)
 
 struct PairSmem {
     uint8_t a[kPStages][kPABytes];
