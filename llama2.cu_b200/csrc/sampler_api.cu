@@ -51,6 +51,10 @@ size_t next_pow2(size_t x) {
 
 // Per-device state for the library-managed buffers.
 struct DeviceCtx {
+    // Serializes the host-buffer entry points on this device: they share the
+    // staging buffers and streams below (distinct Samplers used from
+    // different threads stay independent, as in the reference).
+    std::mutex host_mu;
     int device = -1;
     int num_sms = 0;
     cudaStream_t stream = nullptr;   // used by the single-row llama2.c entry points
@@ -266,6 +270,7 @@ int host_row(float* row, int n, float temperature, float topp, const float* coin
              int force_mode, bool write_back) {
     DeviceCtx* c = nullptr;
     if (get_ctx(&c)) return -1;
+    std::lock_guard<std::mutex> host_lock(c->host_mu);
     if (n < 1 || n > SAMPLER_MAX_VOCAB) {
         fail(SAMPLER_E_UNSUPPORTED, "vocab_size %d outside [1, %d]", n, SAMPLER_MAX_VOCAB);
         return -1;
@@ -564,6 +569,7 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
     DeviceCtx* c = nullptr;
     int rc = get_ctx(&c);
     if (rc) return rc;
+    std::lock_guard<std::mutex> host_lock(c->host_mu);
     const bool all_greedy = !(cfg->flags & SAMPLER_FLAG_PROBS_IN) && cfg->temperature == 0.0f;
     if (!all_greedy && !rng_state) return fail(SAMPLER_E_INVALID, "rng_state is NULL");
     // Each of the two pipeline streams gets its own half of the workspace so

@@ -373,3 +373,22 @@ def test_edge_cases_pipelined(pkg, orc, name, make, temp, topp):
     if nan_rows.any() and 0 < topp < 1:
         assert (out["flags"][nan_rows] & pkg.ROW_NO_CANDIDATE).all()
     check_e2e(orc, out["ids"][keep], ref_ids[keep], ref_p[keep], seeds[keep], np.full(keep.sum(), topp))
+
+
+def test_concurrent_samplers_on_threads(pkg):
+    """Distinct Samplers used from different threads are independent (as in
+    the reference): concurrent sample() calls give the ids a sequential run
+    gives."""
+    from concurrent.futures import ThreadPoolExecutor
+    rows = np.random.default_rng(33).normal(0, 2, (4, 40, 32000)).astype(np.float32)
+
+    def run(t):
+        s = pkg.build_sampler(32000, 0.9, 0.9, 100 + t)
+        ids = [pkg.sample(s, rows[t, r].copy()) for r in range(rows.shape[1])]
+        pkg.free_sampler(s)
+        return ids
+
+    want = [run(t) for t in range(4)]
+    with ThreadPoolExecutor(4) as ex:
+        got = list(ex.map(run, range(4)))
+    assert got == want
