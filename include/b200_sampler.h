@@ -195,6 +195,17 @@ int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* 
                                     const float* topp_rows, const float* coins, unsigned long long* rng_state,
                                     int* out_ids, float* logits_out, int* row_flags, void* stream);
 
+/* The next decode step's input without a host round trip:
+ * out[b, :] = table[ids[b], :] for fp32 table [table_rows, dim] (the token
+ * embedding lookup that starts the reference's forward, llama2.c:636-637),
+ * ids the device ids a sampler call just wrote; an id outside the table
+ * gives a zero row.  Device buffers; asynchronous on `stream`.  With the
+ * library's buffers allocated by a first call, a whole decode step
+ * (sampler_seed_states / classifier_sample_fused / sampler_gather_rows) can
+ * be captured in a CUDA graph. */
+int sampler_gather_rows(const float* table, int table_rows, int dim, const int* ids, int batch, float* out,
+                        void* stream);
+
 /* Largest vocabulary sampler_batched_noalloc accepts. */
 #define SAMPLER_NOALLOC_MAX_VOCAB 32768
 

@@ -23,7 +23,7 @@ EXPORTED_SYMBOLS = [
     "sampler_seed_states", "sampler_last_launch_count", "sampler_last_error", "sampler_shard_rows",
     "sampler_nccl_get_unique_id", "sampler_nccl_comm_init", "sampler_nccl_allgather_ids",
     "sampler_nccl_comm_destroy", "sampler_batched_noalloc", "classifier_sample_fused",
-    "classifier_logits", "rmsnorm_bf16", "classifier_rmsnorm_sample_fused",
+    "classifier_logits", "rmsnorm_bf16", "classifier_rmsnorm_sample_fused", "sampler_gather_rows",
 ]
 
 
@@ -113,6 +113,8 @@ def lib():
     L.classifier_rmsnorm_sample_fused.argtypes = [ctypes.POINTER(SamplerBatchConfig), P, P, P, c_int, c_int, P, P,
                                                   P, P, P, P, P, P]
     L.classifier_rmsnorm_sample_fused.restype = c_int
+    L.sampler_gather_rows.argtypes = [P, c_int, c_int, P, c_int, P, P]
+    L.sampler_gather_rows.restype = c_int
     _lib = L
     return L
 
@@ -248,6 +250,19 @@ def classifier_rmsnorm_sample_fused(x, norm_weight, wcls, temperature, topp, rng
                                                _stream_ptr(stream))
     _check(rc, "classifier_rmsnorm_sample_fused")
     return out_ids
+
+
+def gather_rows(table, ids, out=None, stream=None):
+    """out[b] = table[ids[b]] on the device (float32 table [R, D], int32 ids [B])."""
+    import torch
+    _require_cuda(table, ids, out)
+    R, D = table.shape
+    B = ids.numel()
+    if out is None:
+        out = torch.empty(B, D, dtype=torch.float32, device=table.device)
+    _check(lib().sampler_gather_rows(_ptr(table), R, D, _ptr(ids), B, _ptr(out), _stream_ptr(stream)),
+           "sampler_gather_rows")
+    return out
 
 
 def sample_batched_host(logits_np, temperature, topp, states_np, topp_rows_np=None, probs_in=False):

@@ -615,10 +615,40 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bf16_kernel(const float*
     for (int j = threadIdx.x; j < dim; j += kNormThreads) orow[j] = __float2bfloat16_rn(__fmul_rn(w[j], __fmul_rn(r, xr[j])));
 }
 
+// ---- next-token input: embedding rows of the sampled ids ------------------------
+// x[b, :] = table[ids[b], :] (llama2.c:636-637, the first step of the next
+// forward), so a decode loop feeds the sampled ids back without a host
+// round trip.  One CTA per row, 16-byte copies.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const float* table, int rows, int dim, const int* ids,
+                                                          float* out) {
+    const int b = blockIdx.x;
+    const int id = ids[b];
+    float* dst = out + (long long)b * dim;
+    if (id < 0 || id >= rows) {  // an invalid id gives a zero row
+        for (int j = threadIdx.x; j < dim; j += 256) dst[j] = 0.0f;
+        return;
+    }
+    const float* src = table + (long long)id * dim;
+    if ((dim & 3) == 0) {
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        for (int j = threadIdx.x; j < dim / 4; j += 256) d4[j] = __ldg(s4 + j);
+    } else {
+        for (int j = threadIdx.x; j < dim; j += 256) dst[j] = __ldg(src + j);
+    }
+}
+
 }  // namespace
 
 int launch_rmsnorm_bf16(const float* x, const float* weight, int batch, int dim, void* out, cudaStream_t stream) {
     rmsnorm_bf16_kernel<<<batch, kNormThreads, 0, stream>>>(x, weight, dim, static_cast<__nv_bfloat16*>(out));
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 1 : -(int)e;
+}
+
+int launch_gather_rows(const float* table, int rows, int dim, const int* ids, int batch, float* out,
+                       cudaStream_t stream) {
+    gather_rows_kernel<<<batch, 256, 0, stream>>>(table, rows, dim, ids, out);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 1 : -(int)e;
 }

@@ -529,6 +529,21 @@ int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* 
     return rc;
 }
 
+// Next decode step's input rows from the sampled ids, on the device.
+int sampler_gather_rows(const float* table, int table_rows, int dim, const int* ids, int batch, float* out,
+                        void* stream) {
+    g_last_launches = 0;
+    if (!table || !ids || !out) return fail(SAMPLER_E_INVALID, "null table, ids or out");
+    if (batch < 0 || dim < 1 || table_rows < 1) return fail(SAMPLER_E_INVALID, "bad sizes");
+    if (batch == 0) return SAMPLER_OK;
+    if ((dim & 3) == 0 && (((uintptr_t)table | (uintptr_t)out) & 15u))
+        return fail(SAMPLER_E_INVALID, "table and out must be 16-byte aligned");
+    const int n = b2s::launch_gather_rows(table, table_rows, dim, ids, batch, out, (cudaStream_t)stream);
+    if (n < 0) return fail(SAMPLER_E_CUDA, "gather launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+    g_last_launches = n;
+    return SAMPLER_OK;
+}
+
 // The classifier GEMM alone (no statistics, no sampling).
 int classifier_logits(const void* hidden, const void* wcls, int batch, int dim, int vocab, float* logits_out,
                       void* stream) {

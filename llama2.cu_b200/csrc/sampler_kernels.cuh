@@ -89,5 +89,8 @@ int launch_classifier_gemm_pair(const GemmLaunch& p, int num_sms, cudaStream_t s
 size_t gemm_smem_bytes();
 // Final RMSNorm of `batch` fp32 rows into bf16 (the GEMM's A operand).
 int launch_rmsnorm_bf16(const float* x, const float* weight, int batch, int dim, void* out, cudaStream_t stream);
+// Embedding rows of the sampled ids (the next decode step's input).
+int launch_gather_rows(const float* table, int rows, int dim, const int* ids, int batch, float* out,
+                       cudaStream_t stream);
 
 }  // namespace b2s

@@ -141,3 +141,47 @@ def test_rmsnorm_prologue_and_decode_step(pkg):
     ids2 = pkg.classifier_sample_fused(h, w, 0.8, 0.9, st2)
     torch.cuda.synchronize()
     assert torch.equal(ids1, ids2) and torch.equal(st1, st2)
+
+
+def test_device_resident_decode_loop_in_a_cuda_graph(pkg):
+    """A decode loop whose next input is gathered on the device from the
+    sampled ids (no host sync per token), eagerly and captured once in a CUDA
+    graph and replayed: same ids and states at every step."""
+    B, D, V, steps = 48, 256, 2048, 5
+    g = torch.Generator().manual_seed(41)
+    table = (torch.randn(V, D, generator=g) * 2.0).to(DEV)
+    nw = (1.0 + 0.1 * torch.randn(D, generator=g)).to(DEV)
+    wcls = table.to(torch.bfloat16)  # shared classifier / embedding weights
+    seeds = torch.from_numpy(pkg.workloads.row_seeds(B).view(np.int64).copy()).to(DEV)
+    ids0 = torch.arange(B, dtype=torch.int32, device=DEV) * 37 % V
+
+    def run(step_fn, x, st, ids):
+        out = []
+        for _ in range(steps):
+            step_fn(x, st, ids)
+            out.append(ids.clone())
+        torch.cuda.synchronize()
+        return torch.stack(out).cpu(), st.cpu()
+
+    def step(x, st, ids):
+        pkg.classifier_rmsnorm_sample_fused(x, nw, wcls, 0.9, 0.9, st, out_ids=ids)
+        pkg.gather_rows(table, ids, out=x)
+
+    x = pkg.gather_rows(table, ids0)
+    st = seeds.clone()
+    ids = torch.empty(B, dtype=torch.int32, device=DEV)
+    want_ids, want_st = run(step, x, st, ids)
+
+    x = pkg.gather_rows(table, ids0)
+    st = seeds.clone()
+    ids = torch.empty(B, dtype=torch.int32, device=DEV)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(x, st, ids)
+    x.copy_(pkg.gather_rows(table, ids0))
+    st.copy_(seeds)
+    torch.cuda.synchronize()
+    got_ids, got_st = run(lambda *_: graph.replay(), x, st, ids)
+    assert torch.equal(got_ids, want_ids) and torch.equal(got_st, want_st)
+    assert len(set(want_ids[-1].tolist())) > 1  # the loop really samples
