@@ -365,7 +365,8 @@ __device__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int
 // build_walk_fns (built for n0 >= n keys).  Whole segments and chunks are
 // applied while they stay in one binade and end at or below theta; the chunk
 // that crosses theta or a binade is walked element by element.
-__device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, int n, float theta, float& cum) {
+template <class Get>
+__device__ int walk_fns(const StreamSmem& sm, int n, float theta, float& cum, const Get& get) {
     const int lane = threadIdx.x & 31;
     float s = 0.0f;
     const int nchk = (n + kSC - 1) / kSC;
@@ -419,7 +420,7 @@ __device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, i
                 const int base = (seg * 32 + cpos) * kSC;
                 const int ne = min(kSC, n - base);
                 // the crossing chunk: 32 serial adds (one coalesced load, shuffles)
-                const float x = (lane < ne) ? key_prob(kb[base + lane]) : 0.0f;
+                const float x = (lane < ne) ? get(base + lane) : 0.0f;
                 for (int i = 0; i < ne; ++i) {
                     s = __fadd_rn(s, __shfl_sync(kFullMask, x, i));
                     if (s > theta) {
@@ -433,6 +434,83 @@ __device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, i
     }
     cum = s;
     return n;
+}
+
+__device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, int n, float theta, float& cum) {
+    return walk_fns(sm, n, theta, cum, [&](int i) { return key_prob(kb[i]); });
+}
+
+// ---------------------------------------------------------------------------
+// sample_mult rows (llama2.c:994-1005): the first i with coin < cdf_i, cdf_i
+// the serial fp32 sum of p_j = fl(e_j / S) over j <= i in index order, or
+// n - 1.  The chunk functions of the p's (recomputed exactly from the row)
+// give the cdf; the incoming cdf of each chunk is guessed from pass 1's
+// approximate prefix of e divided by S.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float p_of(const Ctx& c, const StreamSmem& sm, float l, float S, float rS) {
+    const float e = exact_e(c, sm, l);
+    const float q = __fmul_rn(e, rS);
+    return __fmaf_rn(__fmaf_rn(-q, S, e), rS, q);
+}
+
+// All threads: cdf chunk functions for chunks 0..nch-1 (chunk t = elements
+// [32t, 32t + 32) of the row).  gss/sig: pass 1's approximate e prefix and
+// chunk sums of this thread's strips.
+__device__ void build_cdf_fns(StreamSmem& sm, const Ctx& c, float S, const float (&gss)[kStrips],
+                              const float (&sig)[kStrips]) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float rS = __frcp_rn(S);
+    if (tid == 0) sm.n_alt = 0;
+    __syncthreads();
+#pragma unroll 1
+    for (int sidx = 0; sidx < kStrips; ++sidx) {
+        const int t = sidx * kST + tid;
+        const bool valid = t < c.nch;
+        const int cnt = valid ? min(kSC, c.V - t * kSC) : 0;
+        uint32_t alt = 0u;
+        const uint32_t eb = valid ? xm::chain_guess_primary(gss[sidx] * rS, sig[sidx] * rS, alt) : 0u;
+        const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
+        const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
+        float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
+        const float* cp = c.src + t * kSC;
+#pragma unroll 1
+        for (int g = 0; g < kSC / 4; ++g) {
+            if (4 * g >= cnt) break;
+            const float4 q = __ldg(reinterpret_cast<const float4*>(cp + 4 * g));
+            const float a[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const float x = (4 * g + w < cnt) ? p_of(c, sm, a[w], S, rS) : 0.0f;
+                v0 = __fadd_rn(v0, x);
+                v1 = __fadd_rn(v1, x);
+                w0 = __fadd_rn(w0, x);
+                w1 = __fadd_rn(w1, x);
+            }
+        }
+        const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
+        const bool aclean = valid && alt != 0u && (__float_as_uint(w0) >> 23) == alt && (__float_as_uint(w1) >> 23) == alt;
+        const xm::ChainFn f{__fsub_rn(v0, lo), __fsub_rn(v1, lo1),
+                            (__float_as_uint(v0) & 1u) | ((__float_as_uint(v1) & 1u) << 1)};
+        uint32_t z = (clean ? (f.pbits | kFClean) : 0u) | (valid ? kFValid : 0u);
+        if (aclean) {
+            const int ai = atomicAdd(&sm.n_alt, 1);
+            if (ai < kAltCap) {
+                sm.alt[ai] = make_float4(__fsub_rn(w0, alo), __fsub_rn(w1, alo1),
+                                         __uint_as_float((__float_as_uint(w0) & 1u) |
+                                                         ((__float_as_uint(w1) & 1u) << 1) | kFClean),
+                                         __uint_as_float(alt));
+                z |= kFAlt | ((uint32_t)ai << 8);
+            }
+        }
+        if (valid) sm.fn[t] = make_float4(f.L0, f.L1, __uint_as_float(z), __uint_as_float(eb));
+        const uint32_t eb0 = __shfl_sync(kFullMask, eb, 0);
+        const bool uni = __all_sync(kFullMask, !valid || (clean && eb == eb0 && !(z & kFAlt)));
+        const xm::ChainFn F = warp_incl_compose((valid && clean) ? f : xm::chain_identity());
+        if (lane == 31)
+            sm.wfn[sidx * kSW + warp] =
+                make_float4(F.L0, F.L1, __uint_as_float(F.pbits | (uni ? kFClean : 0u)), __uint_as_float(eb0));
+    }
+    __syncthreads();
 }
 
 // Sorts every bin 0..D of the scattered nucleus by (e desc, index asc).  Warps
@@ -599,10 +677,9 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
         c.T = p.temperature_rows ? p.temperature_rows[row] : p.temperature;
         const float topp = p.topp_rows ? p.topp_rows[row] : p.topp;
         const bool greedy = (c.T == 0.0f);
-        if (!greedy && (topp <= 0.0f || topp >= 1.0f)) {  // sample_mult rows: general kernel
-            if (tid == 0) defer_row_s(p, row);
-            continue;
-        }
+        // sample_mult rows (topp outside (0, 1), llama2.c:1098-1100) share the
+        // passes and take the cdf walk at the end
+        const bool mult = !greedy && (topp <= 0.0f || topp >= 1.0f);
 
         if (greedy) {
             // first index of the strict max, NaN at index 0 wins (llama2.c:981-992)
@@ -839,7 +916,27 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
         }
         int flags = 0, id = 0;
         bool defer = false;
-        if (row_nan) {
+        if (mult) {
+            if (row_nan) {
+                defer = true;  // NaN rows of sample_mult: the general kernel
+            } else {
+                if (warp == 0) {
+                    const float S = resolve_S(sm, c);
+                    if (lane == 0) sm.fval = S;
+                }
+                __syncthreads();
+                const float S = sm.fval;
+                build_cdf_fns(sm, c, S, gss, sig);
+                if (warp == 0) {
+                    const float rS = __frcp_rn(S);
+                    float cdf = 0.0f;
+                    const int k = walk_fns(sm, V, coin, cdf, [&](int i) { return p_of(c, sm, __ldg(c.src + i), S, rS); });
+                    if (lane == 0) sm.result = (k < V) ? k : V - 1;  // llama2.c:1004
+                }
+                __syncthreads();
+                id = sm.result;
+            }
+        } else if (row_nan) {
             flags = kFlagNan | kFlagNoCand;
         } else {
             // ---- nucleus bins from the histogram: guaranteed mass of bins 0..D

@@ -143,6 +143,21 @@ def test_mult_workload_end_to_end(pkg, orc, golden):
     check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, np.ones(1024))
 
 
+def test_mult_workload_streamed(pkg, orc, golden):
+    """Without probability write-back, sample_mult rows take the streaming
+    kernel's cdf walk (chunk functions of the exact p's)."""
+    w = pkg.workloads.mult()
+    seeds = pkg.workloads.row_seeds(1024)
+    out = gpu_sample(pkg, w["logits"], w["temperature"], w["topp"], seeds=seeds)
+    ref_ids, ref_st, ref_p = orc.sample_batch(w["logits"], w["temperature"], w["topp"], seeds, probs_out=True)
+    assert ref_ids.tolist() == golden["mult"]["ids"]
+    assert np.array_equal(out["states"], ref_st)
+    check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, np.ones(1024))
+    small = out["ids"][:64]  # the 1024-thread shape (batch below the SM count) on the same rows
+    out64 = gpu_sample(pkg, w["logits"][:64], w["temperature"], w["topp"], seeds=seeds[:64])
+    assert np.array_equal(out64["ids"], small)
+
+
 def test_topp_workload_end_to_end(pkg, orc, golden):
     w = pkg.workloads.topp()
     seeds = pkg.workloads.row_seeds(4096)
