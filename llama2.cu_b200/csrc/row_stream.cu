@@ -35,9 +35,12 @@
 //     to topp and then to r = coin*cum.  A walk that does not cross topp
 //     inside the selected bins (S_approx was off by more than the margin)
 //     defers the row.
-// Rows this kernel does not finish (sample_mult rows, nuclei above the
-// on-chip capacity, failed guesses without stored values) are appended to
-// the deferred-row list that the general row kernel processes next.
+// sample_mult rows share the passes and the resolution of S, then walk the
+// cdf by chunk functions of the exact probabilities.
+// Rows this kernel does not finish (extreme temperatures or logits, NaN rows
+// of sample_mult, bins of more than 256 keys, walks whose S_approx margin
+// failed) are appended to the deferred-row list that the general row kernel
+// processes next.
 #include "device_common.cuh"
 #include "exact_math.cuh"
 #include "sampler_kernels.cuh"

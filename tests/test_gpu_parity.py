@@ -187,8 +187,7 @@ def test_topp_workload_pipelined_path(pkg, orc, golden):
 
 def test_mixed_modes_in_one_batch(pkg, orc):
     """Greedy, top-p and multinomial rows together (per-row temperature and
-    topp): the pipelined kernel takes greedy and top-p rows and defers the
-    multinomial ones."""
+    topp), all on the streaming kernel."""
     rng = np.random.default_rng(41)
     B = 300
     x = rng.normal(0, 2.5, (B, 32000)).astype(np.float32)
