@@ -1035,21 +1035,39 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                     }
                     // padding (-inf * sg) never passes for T > 0; for T < 0 it
                     // is excluded by the granule bound below
-                    while (m) {
+                    // two elements per round: independent chains overlap
+                    auto take = [&](int& idx, float& e) {
+                        idx = -1;
+                        e = 0.0f;
+                        if (!m) return;
                         const int j = __ffs(m) - 1;
                         m &= m - 1;
                         const int gi = g0 + (j >> 2) * nu;
-                        if (gi >= ng) continue;
-                        const int idx = 4 * gi + (j & 3);
-                        const float d = __fsub_rn(div_lean(__ldg(c.src + idx), c), c.max_x);
-                        if (d >= d_cand) {
-                            const float e = xm::exp_f32(d, sm.exptab);
-                            if (e >= e_min) {
-                                const int b = bin_of(e);
-                                if (b <= D) {
-                                    const int pos = atomicAdd(&sm.hist[b], 1);
-                                    if (pos < K) kb[pos] = cand_key(e, idx);
-                                }
+                        if (gi < ng) idx = 4 * gi + (j & 3);
+                    };
+                    while (m) {
+                        int i1, i2;
+                        float e1, e2;
+                        take(i1, e1);
+                        take(i2, e2);
+                        const float l1 = (i1 >= 0) ? __ldg(c.src + i1) : 0.0f;
+                        const float l2 = (i2 >= 0) ? __ldg(c.src + i2) : 0.0f;
+                        const float d1 = __fsub_rn(div_lean(l1, c), c.max_x);
+                        const float d2 = __fsub_rn(div_lean(l2, c), c.max_x);
+                        if (i1 >= 0 && d1 >= d_cand) e1 = xm::exp_f32(d1, sm.exptab);
+                        if (i2 >= 0 && d2 >= d_cand) e2 = xm::exp_f32(d2, sm.exptab);
+                        if (i1 >= 0 && e1 >= e_min) {
+                            const int b = bin_of(e1);
+                            if (b <= D) {
+                                const int pos = atomicAdd(&sm.hist[b], 1);
+                                if (pos < K) kb[pos] = cand_key(e1, i1);
+                            }
+                        }
+                        if (i2 >= 0 && e2 >= e_min) {
+                            const int b = bin_of(e2);
+                            if (b <= D) {
+                                const int pos = atomicAdd(&sm.hist[b], 1);
+                                if (pos < K) kb[pos] = cand_key(e2, i2);
                             }
                         }
                     }
