@@ -447,8 +447,11 @@ __device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, i
 // give the cdf; the incoming cdf of each chunk is guessed from pass 1's
 // approximate prefix of e divided by S.
 // ---------------------------------------------------------------------------
+// p = fl(e/S): Markstein division where it is correctly rounded (S in
+// [1, 2^15], e >= 2^-60), IEEE division below (tiny and subnormal quotients).
 __device__ __forceinline__ float p_of(const Ctx& c, const StreamSmem& sm, float l, float S, float rS) {
     const float e = exact_e(c, sm, l);
+    if (!(e >= 0x1p-60f)) return __fdiv_rn(e, S);
     const float q = __fmul_rn(e, rS);
     return __fmaf_rn(__fmaf_rn(-q, S, e), rS, q);
 }
@@ -457,7 +460,7 @@ __device__ __forceinline__ float p_of(const Ctx& c, const StreamSmem& sm, float 
 // [32t, 32t + 32) of the row).  gss/sig: pass 1's approximate e prefix and
 // chunk sums of this thread's strips.
 __device__ void build_cdf_fns(StreamSmem& sm, const Ctx& c, float S, const float (&gss)[kStrips],
-                              const float (&sig)[kStrips]) {
+                              const float (&sig)[kStrips], float* probs_row) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float rS = __frcp_rn(S);
     if (tid == 0) sm.n_alt = 0;
@@ -478,14 +481,18 @@ __device__ void build_cdf_fns(StreamSmem& sm, const Ctx& c, float S, const float
             if (4 * g >= cnt) break;
             const float4 q = __ldg(reinterpret_cast<const float4*>(cp + 4 * g));
             const float a[4] = {q.x, q.y, q.z, q.w};
+            float pv[4];
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
                 const float x = (4 * g + w < cnt) ? p_of(c, sm, a[w], S, rS) : 0.0f;
+                pv[w] = x;
                 v0 = __fadd_rn(v0, x);
                 v1 = __fadd_rn(v1, x);
                 w0 = __fadd_rn(w0, x);
                 w1 = __fadd_rn(w1, x);
             }
+            if (probs_row)  // the softmax sample() leaves in the buffer (cnt is a multiple of 4)
+                reinterpret_cast<float4*>(probs_row + t * kSC)[g] = make_float4(pv[0], pv[1], pv[2], pv[3]);
         }
         const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
         const bool aclean = valid && alt != 0u && (__float_as_uint(w0) >> 23) == alt && (__float_as_uint(w1) >> 23) == alt;
@@ -691,6 +698,12 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 float a[kSC];
                 load_chunk(c, t, a);
                 const int cnt = min(kSC, V - t * kSC);
+                if (p.probs_out) {  // sample() leaves the logits in place when greedy
+                    float4* dst = reinterpret_cast<float4*>(p.probs_out + (long long)row * V + t * kSC);
+#pragma unroll
+                    for (int g = 0; g < kSC / 4; ++g)
+                        if (4 * g < cnt) dst[g] = make_float4(a[4 * g], a[4 * g + 1], a[4 * g + 2], a[4 * g + 3]);
+                }
 #pragma unroll
                 for (int j = 0; j < kSC; ++j)
                     if (j < cnt && (a[j] > bv || (a[j] == bv && t * kSC + j < bi))) {
@@ -926,7 +939,7 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 }
                 __syncthreads();
                 const float S = sm.fval;
-                build_cdf_fns(sm, c, S, gss, sig);
+                build_cdf_fns(sm, c, S, gss, sig, p.probs_out ? p.probs_out + (long long)row * V : nullptr);
                 if (warp == 0) {
                     const float rS = __frcp_rn(S);
                     float cdf = 0.0f;
@@ -937,6 +950,7 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 id = sm.result;
             }
         } else if (row_nan) {
+            if (p.probs_out) defer = true;  // the general kernel writes the NaN probabilities
             flags = kFlagNan | kFlagNoCand;
         } else {
             // ---- nucleus bins from the histogram: guaranteed mass of bins 0..D
@@ -1077,6 +1091,18 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
             }
             __syncthreads();
             const float S = sm.fval;
+            if (p.probs_out && !(!fits || sm.flag)) {
+                // the softmax sample() leaves in the buffer: p = fl(e/S) for
+                // every element (V is a multiple of 4 on this kernel)
+                const float rS = __frcp_rn(S);
+                const float4* src4 = reinterpret_cast<const float4*>(c.src);
+                float4* dst4 = reinterpret_cast<float4*>(p.probs_out + (long long)row * V);
+                for (int g = tid; g < V / 4; g += kST) {
+                    const float4 q = __ldg(src4 + g);
+                    dst4[g] = make_float4(p_of(c, sm, q.x, S, rS), p_of(c, sm, q.y, S, rS), p_of(c, sm, q.z, S, rS),
+                                          p_of(c, sm, q.w, S, rS));
+                }
+            }
             if (!fits || sm.flag) {
                 defer = true;
             } else {

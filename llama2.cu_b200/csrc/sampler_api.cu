@@ -162,7 +162,7 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
              const float* temperature_rows, const float* topp_rows, const float* coins,
              unsigned long long* rng_state, int* out_ids, float* probs_out, int* row_flags,
              void* workspace, size_t workspace_bytes, cudaStream_t stream, int force_mode,
-             const float4* stats = nullptr, long long stats_ld = 0) {
+             const float4* stats = nullptr, long long stats_ld = 0, bool allow_stream = true) {
     g_last_launches = 0;
     if (!cfg || !logits || !out_ids) return fail(SAMPLER_E_INVALID, "null config, logits or out_ids");
     const int V = cfg->vocab_size;
@@ -228,11 +228,12 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
     p.error_word = c->error_word;
     p.defer_count = defer_count;
     p.defer_rows = defer_rows;
-    // Fast path: the streaming kernel takes greedy and top-p rows and defers
-    // the rest to the general kernel, which then walks the deferred list.
-    // Probabilities in/out and forced modes use the general kernel for every
-    // row.
-    const bool streamed = !probs_in && !probs_out && force_mode == 0 && stream_layout_ok(logits, V, ld);
+    // Fast path: the streaming kernel takes greedy, top-p and sample_mult rows
+    // (writing the probabilities when asked) and defers the rest to the
+    // general kernel, which then walks the deferred list.  Probabilities in
+    // and forced modes use the general kernel for every row.
+    const bool streamed = allow_stream && !probs_in && force_mode == 0 && stream_layout_ok(logits, V, ld) &&
+                          ((uintptr_t)probs_out & 15u) == 0;
     int launches = 0;
     if (streamed) {
         B2S_CUDA(cudaMemsetAsync(defer_count, 0, sizeof(int), stream));
@@ -286,8 +287,11 @@ int host_row(float* row, int n, float temperature, float topp, const float* coin
         return -1;
     }
     SamplerBatchConfig cfg{n, temperature, topp, probs_in ? SAMPLER_FLAG_PROBS_IN : 0};
+    // one row with its probabilities: the general kernel's single pass is the
+    // lower latency here
     const int rc = dispatch(&cfg, c->d_row, 1, n, nullptr, nullptr, coin ? c->d_coin : nullptr, nullptr, c->d_id,
-                            write_back ? c->d_probs : nullptr, nullptr, nullptr, 0, s, force_mode);
+                            write_back ? c->d_probs : nullptr, nullptr, nullptr, 0, s, force_mode, nullptr, 0,
+                            !write_back);
     if (rc) return -1;
     int id = -1;
     if (cudaMemcpyAsync(&id, c->d_id, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
