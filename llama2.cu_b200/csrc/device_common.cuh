@@ -248,6 +248,34 @@ __device__ void warp_sort_bin(unsigned long long* seg, int n, int lane) {
     }
 }
 
+// Two bins of 1..32 keys each (not the last bin; indices < 2^15 - 1) sorted
+// together: the two 32-key networks run in lockstep so their shuffle
+// latencies overlap.
+__device__ void warp_sort_bin_pair(unsigned long long* sa, int na, unsigned long long* sb, int nb, int lane) {
+    auto k32 = [](unsigned long long key) {
+        return ((((uint32_t)(key >> 32)) & 0x1FFFFu) << 15) | (uint32_t)(0x7FFF - key_index(key));
+    };
+    const unsigned long long a0 = (lane < na) ? sa[lane] : 0ull;
+    const unsigned long long b0 = (lane < nb) ? sb[lane] : 0ull;
+    const uint32_t ta = __shfl_sync(kFullMask, (uint32_t)(a0 >> 32) >> 17, 0);
+    const uint32_t tb = __shfl_sync(kFullMask, (uint32_t)(b0 >> 32) >> 17, 0);
+    uint32_t ka = (lane < na) ? k32(a0) : 0u;
+    uint32_t kb = (lane < nb) ? k32(b0) : 0u;
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const uint32_t oa = __shfl_xor_sync(kFullMask, ka, stride);
+            const uint32_t ob = __shfl_xor_sync(kFullMask, kb, stride);
+            const bool take_max = ((lane & stride) == 0) == ((lane & size) == 0);
+            ka = take_max ? max(ka, oa) : min(ka, oa);
+            kb = take_max ? max(kb, ob) : min(kb, ob);
+        }
+    }
+    if (lane < na) sa[lane] = cand_key(__uint_as_float((ta << 17) | (ka >> 15)), 0x7FFF - (int)(ka & 0x7FFFu));
+    if (lane < nb) sb[lane] = cand_key(__uint_as_float((tb << 17) | (kb >> 15)), 0x7FFF - (int)(kb & 0x7FFFu));
+}
+
 
 
 }  // namespace

@@ -543,6 +543,7 @@ __device__ void sort_bins(StreamSmem& sm, unsigned long long* kb, int D, int K, 
         }
         unsigned todo = __ballot_sync(kFullMask, n >= 2 && n <= 256 && s0 >= 0 && s0 + n <= K);
         const unsigned small = __ballot_sync(kFullMask, n <= 16);
+        const unsigned mid = __ballot_sync(kFullMask, n > 16 && n <= 32);
         while (todo) {
             const int src = __ffs(todo) - 1;
             todo &= todo - 1;
@@ -580,9 +581,19 @@ __device__ void sort_bins(StreamSmem& sm, unsigned long long* kb, int D, int K, 
                 __syncwarp();
                 if (hl < my_nn) kb[my_ss + rank] = key;
                 __syncwarp();
+            } else if (narrow && nn <= 32) {
+                // pair it with the next bin of 17..32 keys, if any
+                const unsigned rest = todo & mid;
+                const int src2 = rest ? (__ffs(rest) - 1) : -1;
+                if (src2 >= 0 && b0 + src2 < kBins - 1) {
+                    todo &= ~(1u << src2);
+                    warp_sort_bin_pair(seg, nn, kb + __shfl_sync(kFullMask, s0, src2), __shfl_sync(kFullMask, n, src2),
+                                       lane);
+                } else {
+                    warp_sort_bin<1>(seg, nn, lane);
+                }
             } else if (narrow) {
-                if (nn <= 32) warp_sort_bin<1>(seg, nn, lane);
-                else if (nn <= 64) warp_sort_bin<2>(seg, nn, lane);
+                if (nn <= 64) warp_sort_bin<2>(seg, nn, lane);
                 else if (nn <= 128) warp_sort_bin<4>(seg, nn, lane);
                 else warp_sort_bin<8>(seg, nn, lane);
             } else {
