@@ -158,7 +158,8 @@ const char* sampler_last_error(void);
  * llama2_cublas_bf16.cu:411) followed by sample() on the host
  * (llama2_cublas.cu:5831-5905), for `batch` rows at once:
  *   logits[b, v] = sum_k hidden[b, k] * wcls[v, k]   (bf16 in, fp32 accumulate)
- * on the sm_100a tensor cores, whose epilogue also emits the per-row softmax
+ * on the sm_100a tensor cores (for one or two rows: a CUDA-core GEMV that
+ * streams wcls once), whose epilogue also emits the per-row softmax
  * statistics the sampler needs, then per row exactly what sampler_batched()
  * does on those logits (same ids, states and flags).
  *   hidden     bf16 [batch, dim] row-major (16-byte aligned), dim % 8 == 0

@@ -8,10 +8,10 @@
 // (llama2_cublas.cu:5825-5826 cublasSgemv of wcls, llama2_cublas_bf16.cu:411
 // the bf16 GemmEx form), at batch B instead of one token.
 //
-// Two persistent kernels: for batches above 128 rows, CTA pairs with 256 x 256
-// tiles (tcgen05 cta_group::2, described with that kernel below); for decode
-// batches, one 256-thread CTA per SM with tile 128 (rows of H) x 256
-// (vocabulary entries), K step 64:
+// Two persistent tensor-core kernels: for batches above 128 rows, CTA pairs
+// with 256 x 256 tiles (tcgen05 cta_group::2, described with that kernel
+// below); for 3 to 128 rows, one 256-thread CTA per SM with tile 128 (rows of
+// H) x 256 (vocabulary entries), K step 64:
 //   warp 0     TMA producer: A [128 x 64] and B [256 x 64] bf16 boxes, 128-byte
 //              swizzle, into a 4-stage ring (48 KB a stage)
 //   warp 1     MMA issuer (one thread): four tcgen05.mma (M128 N256 K16) per
@@ -21,7 +21,8 @@
 //   warps 4-7  epilogue: tcgen05.ld of 32 columns at a time (one row per
 //              thread), fp32 logits to HBM and, per 32-column chunk, the
 //              statistics (max, min, approximate sum of exp((l - max)/T))
-// Every CTA loads its own tiles from this GPU's memory with plain TMA loads
+// One or two rows take a CUDA-core GEMV (below) that streams W at the HBM
+// rate.  Every CTA loads its own tiles from this GPU's memory with plain TMA loads
 // (the kernels also run on every GPU of a multi-GPU job).  Every mbarrier
 // wait is bounded; a timeout sets the error word and drains the pipeline.
 #include "device_common.cuh"
@@ -160,6 +161,28 @@ __device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int& m_blk
     m_blk = g * kGroupM + (r - n_blk * gm);
 }
 
+// Statistics of one 32-column chunk of a row (the streaming sampler's pass 1
+// on the same values): max l, min l, and the approximate sum of
+// exp2(l*k2 - max(l*k2)) with k2 = log2(e)/T, in column order (0 when T = 0).
+__device__ __forceinline__ float4 chunk_stats(const float (&v)[32], float T) {
+    float mx = v[0], mn = v[0];
+#pragma unroll
+    for (int j = 1; j < 32; ++j) {
+        mx = fmaxf(mx, v[j]);
+        mn = fminf(mn, v[j]);
+    }
+    float s2 = 0.0f;
+    if (T != 0.0f) {
+        const float k2 = __frcp_rn(T) * 1.4426950408889634f;
+        float m2 = -3.4e38f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m2 = fmaxf(m2, v[j] * k2);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s2 += ex2_approx(__fmaf_rn(v[j], k2, -m2));
+    }
+    return make_float4(mx, mn, s2, 0.0f);
+}
+
 // Epilogue of one warp: 256 accumulator columns of this thread's TMEM lane
 // (row `row`, vocabulary columns col0 ..), 32 at a time: fp32 logits to HBM
 // and, per 32-column chunk, the streaming sampler's pass-1 statistics.
@@ -167,7 +190,6 @@ __device__ __forceinline__ void epilogue_rows(const GemmLaunch& p, uint32_t lane
     const bool row_ok = row < p.batch;
     float T = p.temperature;
     if (p.temperature_rows && row_ok) T = p.temperature_rows[row];
-    const float k2 = __frcp_rn(T) * 1.4426950408889634f;
 #pragma unroll 1
     for (int c = 0; c < kGN / 32; ++c) {
         float v[32];
@@ -177,23 +199,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmLaunch& p, uint32_t lane
             float4* dst = reinterpret_cast<float4*>(p.logits + (long long)row * p.ld + col);
 #pragma unroll
             for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            if (p.stats) {
-                float mx = v[0], mn = v[0];
-#pragma unroll
-                for (int j = 1; j < 32; ++j) {
-                    mx = fmaxf(mx, v[j]);
-                    mn = fminf(mn, v[j]);
-                }
-                float s2 = 0.0f;
-                if (T != 0.0f) {
-                    float m2 = -3.4e38f;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) m2 = fmaxf(m2, v[j] * k2);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) s2 += ex2_approx(__fmaf_rn(v[j], k2, -m2));
-                }
-                p.stats[(long long)row * p.stats_ld + col / 32] = make_float4(mx, mn, s2, 0.0f);
-            }
+            if (p.stats) p.stats[(long long)row * p.stats_ld + col / 32] = chunk_stats(v, T);
         }
     }
 }
@@ -557,6 +563,144 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
     }
 }
 
+// ---- decode batches: a bandwidth-bound GEMV -------------------------------------
+// With B <= kGemvMaxBatch rows the classifier is a stream of W (V*D*2 bytes,
+// 262 MB at 32000 x 4096) with B multiply-adds per element: no operand reuse
+// for the tensor cores to exploit, so CUDA cores read W once, with 16-byte
+// streaming loads, at the HBM rate (B = 1: about 45 us for 262 MB, against
+// about 58 us for the single-CTA tensor-core kernel's 128-row tile).  One CTA
+// of kVWarps warps per 32 vocabulary rows (one statistics chunk), all CTAs
+// resident at once: warp w takes the 256-element K steps w, w + kVWarps, ..
+// of kVRows rows at a time, two steps (2 x kVRows 16-byte loads) in flight
+// per lane.  Lane partial sums are reduced across the warp (reduce-scatter,
+// then butterfly) and then across the warps in a fixed order; warp 0 writes
+// the logits and the chunk statistics exactly as the tensor-core epilogue
+// does.
+#ifndef B2S_GEMV_MAX_BATCH
+#define B2S_GEMV_MAX_BATCH 2
+#endif
+constexpr int kGemvMaxBatch = B2S_GEMV_MAX_BATCH;
+static_assert(kGemvMaxBatch >= 0 && kGemvMaxBatch <= 2, "the GEMV kernel takes up to two rows");
+constexpr int kVWarps = 4;
+constexpr int kVRows = 4;  // rows of W per pass of a warp
+
+// d = a * b + c for bf16 halves a, b of packed words (fma.rn.f32.bf16: the
+// product of two bf16 values is exact in fp32, so this equals the fp32 FMA of
+// the widened values).
+__device__ __forceinline__ float fma_bf16_lo(uint32_t a2, uint32_t b2, float c) {
+    float d;
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, al, bl, %3;\n\t}" : "=f"(d) : "r"(a2), "r"(b2), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float fma_bf16_hi(uint32_t a2, uint32_t b2, float c) {
+    float d;
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, ah, bh, %3;\n\t}" : "=f"(d) : "r"(a2), "r"(b2), "f"(c));
+    return d;
+}
+
+// acc[r][b] += W[row r, 8 elements] . H[b, same 8 elements] for one K step,
+// element by element in K order.
+template <int NB>
+__device__ __forceinline__ void gemv_step(float (&acc)[kVRows][NB], const uint4 (&w)[kVRows], const uint4* h,
+                                          long long rs, int batch) {
+    uint32_t hq[NB][4];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        const uint4 q = (b < batch) ? __ldg(h + b * rs) : make_uint4(0u, 0u, 0u, 0u);
+        hq[b][0] = q.x;
+        hq[b][1] = q.y;
+        hq[b][2] = q.z;
+        hq[b][3] = q.w;
+    }
+#pragma unroll
+    for (int r = 0; r < kVRows; ++r) {
+        const uint32_t wq[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                acc[r][b] = fma_bf16_lo(wq[e], hq[b][e], acc[r][b]);
+                acc[r][b] = fma_bf16_hi(wq[e], hq[b][e], acc[r][b]);
+            }
+    }
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kVWarps * 32, 8) classifier_gemv_kernel(GemmLaunch p) {
+    __shared__ float part[kVWarps][NB][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int v0 = blockIdx.x * 32;
+    const long long rs = p.dim >> 3;  // uint4 per row (dim % 8 == 0)
+    const int steps = (p.dim + 255) >> 8;
+    const uint4* W = reinterpret_cast<const uint4*>(p.w);
+    const uint4* H = reinterpret_cast<const uint4*>(p.h) + lane;
+    const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1;
+    float mine[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) mine[b] = 0.0f;
+#pragma unroll 1
+    for (int g = 0; g < 32 / kVRows; ++g) {
+        const uint4* wr = W + (long long)(v0 + g * kVRows) * rs + lane;
+        float acc[kVRows][NB];
+#pragma unroll
+        for (int r = 0; r < kVRows; ++r)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) acc[r][b] = 0.0f;
+#pragma unroll 1
+        for (int s = warp; s < steps; s += 2 * kVWarps) {
+            const int s2 = s + kVWarps;
+            const bool ok1 = s * 32 + lane < rs;
+            const bool ok2 = s2 < steps && s2 * 32 + lane < rs;
+            uint4 w1[kVRows], w2[kVRows];
+#pragma unroll
+            for (int r = 0; r < kVRows; ++r) {
+                w1[r] = ok1 ? __ldcs(wr + r * rs + s * 32) : make_uint4(0u, 0u, 0u, 0u);
+                w2[r] = ok2 ? __ldcs(wr + r * rs + s2 * 32) : make_uint4(0u, 0u, 0u, 0u);
+            }
+            if (ok1) gemv_step<NB>(acc, w1, H + s * 32, rs, p.batch);
+            if (ok2) gemv_step<NB>(acc, w2, H + s2 * 32, rs, p.batch);
+        }
+        // rows r of this pass: lanes with bits (4, 3) = (r >> 1, r & 1) end
+        // with the warp's full sum of row r
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            float k0 = b4 ? acc[2][b] : acc[0][b], k1 = b4 ? acc[3][b] : acc[1][b];
+            const float x0 = b4 ? acc[0][b] : acc[2][b], x1 = b4 ? acc[1][b] : acc[3][b];
+            k0 += __shfl_xor_sync(kFullMask, x0, 16);
+            k1 += __shfl_xor_sync(kFullMask, x1, 16);
+            float kk = b3 ? k1 : k0;
+            kk += __shfl_xor_sync(kFullMask, b3 ? k0 : k1, 8);
+            kk += __shfl_xor_sync(kFullMask, kk, 4);
+            kk += __shfl_xor_sync(kFullMask, kk, 2);
+            kk += __shfl_xor_sync(kFullMask, kk, 1);
+            if ((lane & 7) == g) mine[b] = kk;
+        }
+    }
+    const int j = kVRows * (lane & 7) + 2 * b4 + b3;  // the vocabulary row this lane holds
+#pragma unroll
+    for (int b = 0; b < NB; ++b) part[warp][b][j] = mine[b];
+    __syncthreads();
+    if (warp != 0) return;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        float v = part[0][b][lane];
+#pragma unroll
+        for (int w = 1; w < kVWarps; ++w) v = __fadd_rn(v, part[w][b][lane]);
+        part[0][b][lane] = v;
+        if (b < p.batch) p.logits[(long long)b * p.ld + v0 + lane] = v;
+    }
+    __syncwarp();
+    if (p.stats && lane < NB && lane < p.batch) {
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = part[0][lane][c];
+        const float T = p.temperature_rows ? p.temperature_rows[lane] : p.temperature;
+        p.stats[(long long)lane * p.stats_ld + blockIdx.x] = chunk_stats(v, T);
+    }
+}
+
 // ---- host: tensor maps -------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -678,7 +822,22 @@ int launch_classifier_gemm_pair(const GemmLaunch& p, int num_sms, cudaStream_t s
     return e == cudaSuccess ? 1 : -(int)e;
 }
 
+int launch_classifier_gemv(const GemmLaunch& p, cudaStream_t stream) {
+    if (p.batch < 1 || p.batch > kGemvMaxBatch || (p.dim & 7) || (p.vocab & 31) ||
+        ((reinterpret_cast<uintptr_t>(p.h) | reinterpret_cast<uintptr_t>(p.w)) & 15))
+        return -(int)cudaErrorInvalidValue;
+    const int grid = p.vocab / 32;
+    if (p.batch == 1)
+        classifier_gemv_kernel<1><<<grid, kVWarps * 32, 0, stream>>>(p);
+    else
+        classifier_gemv_kernel<2><<<grid, kVWarps * 32, 0, stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 1 : -(int)e;
+}
+
 int launch_classifier_gemm(const GemmLaunch& p, int num_sms, cudaStream_t stream) {
+    // One or two rows stream W on CUDA cores.
+    if (p.batch <= kGemvMaxBatch) return launch_classifier_gemv(p, stream);
     // Batches of more than one 128-row block use CTA pairs (half the staged
     // bytes per FLOP: 1386 vs 1297 TFLOP/s at 8192 x 4096 x 32000); a single
     // block (decode batches) is faster on single CTAs, whose 125 N tiles

@@ -65,8 +65,10 @@ def check_logits(h, w, logits):
 
 
 # (B, D, V): the decode shape with fewer rows, then tails in every dimension
-# (rows % 128, dim % 64, vocab % 256)
-SHAPES = [(256, 4096, 32000), (300, 4096, 4064), (130, 520, 32000), (1, 64, 256)]
+# (rows % 128, dim % 64, vocab % 256); one or two rows take the CUDA-core
+# GEMV (dim % 256 tails included), three rows the smallest tensor-core tile
+SHAPES = [(256, 4096, 32000), (300, 4096, 4064), (130, 520, 32000), (1, 64, 256), (1, 4096, 32000),
+          (2, 4104, 32000), (2, 520, 4064), (3, 4096, 32000)]
 
 
 @pytest.mark.parametrize("B,D,V", SHAPES)
