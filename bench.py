@@ -357,12 +357,35 @@ def run_decode(args):
                 fn()
             res[name] = (time.perf_counter() - t0) / args.steps * 1e6
         out["greedy" if temp == 0.0 else "topp"] = dict(ours_us=res["ours"], reference_path_us=res["reference_path"])
+    # the classifier alone (classifier_gemv_kernel at one row), device-timed on
+    # its stream; W (262 MB) is larger than the 126 MB L2, so no flush
+    stream = torch.cuda.current_stream()
+    lg = torch.empty(1, V, device=dev)
+    for _ in range(5):
+        pkg.classifier_logits(h, w, logits_out=lg, stream=stream)
+    n_cls = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n_cls):
+        pkg.classifier_logits(h, w, logits_out=lg, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    cls_us = e0.elapsed_time(e1) / n_cls * 1e3
+    peaks = load_json(os.path.join(ROOT, "MEASURED_PEAKS.json"), {})
+    peak, peak_note = peaks.get("hbm_gbs"), "of measured"
+    if not peak:
+        peak, peak_note = 6650.0, "of fallback"
+    alg_bytes = V * D * 2 + D * 2 + V * 4  # wcls + hidden row + fp32 logits
+    achieved = alg_bytes / (cls_us * 1e-6) / 1e9
+    roof = dict(bound="hbm", kernel="classifier_gemv_kernel", achieved=achieved, peak=peak, unit="GB/s",
+                frac=achieved / peak, traffic=profiled_traffic("classifier_gemv_kernel_decode_1x4096x32000.md"),
+                note=f"{peak_note} HBM copy bandwidth; {cls_us:.1f} us per call")
     line = dict(metric="decode step latency at batch 1 (classifier + sampling), us", value=out["topp"]["ours_us"],
                 unit="us", n_gpus=1, steps=args.steps, warmup=args.warmup, higher_is_better=False,
                 vs_baseline=None, dtype="bf16", data="synthetic (seeded numpy PCG64)",
                 config=dict(workload=f"decode: hidden bf16 [1,{D}] x wcls [{V},{D}], T={f['temperature']}, "
                                      f"topp {f['topp']}; greedy T=0"),
-                latency=out, reference_kind=kind,
+                latency=out, reference_kind=kind, roofline=roof,
                 reference_path="torch.mv fp32 wcls (cuBLAS GEMV) + 128 KB D2H + reference sample() on one host thread")
     print(json.dumps(line), flush=True)
     return 0

@@ -207,7 +207,8 @@ def classifier_sample_fused(hidden, wcls, temperature, topp, rng_state=None, *, 
 
 
 def classifier_logits(hidden, wcls, logits_out=None, stream=None):
-    """logits = hidden . wcls^T on the tensor cores (bf16 in, fp32 out)."""
+    """logits = hidden . wcls^T (bf16 in, fp32 out): tensor cores from three rows,
+    a CUDA-core GEMV streaming wcls for one or two."""
     import torch
     _require_cuda(hidden, wcls, logits_out)
     B, D = hidden.shape
