@@ -864,7 +864,9 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
 
         // ---- pass 2: exact e where it matters, chunk functions, histogram
         const float cutoff = __fdiv_rn(__fsub_rn(1.0f, topp), (float)(V - 1));  // llama2.c:1024
-        const float e_min = cutoff * s_approx * 0.9921875f;
+        // candidates counted in the histogram: e >= e_min (none for
+        // sample_mult rows, whose cutoff would count every element)
+        const float e_min = mult ? INFINITY : cutoff * s_approx * 0.9921875f;
         const float d_cand = (e_min > 0.0f) ? __logf(e_min) - 1e-3f : -INFINITY;
         // every d = fl(x - max) lies in [fl(min_x - max_x), 0]: rows whose
         // range stays inside the fast exp range skip the range check
