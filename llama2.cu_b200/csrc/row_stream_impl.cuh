@@ -45,6 +45,12 @@ struct StreamSmem {
     int result;
     int n0;
     float fval;
+    // running sums of the first nucleus walk (cum > topp), where the second
+    // (r < cdf, the same serial sums) may resume: at segment starts (chunk
+    // walk) or at chain steps (ck_pos = element index)
+    float ck_s[32];
+    int ck_pos[32];
+    int n_ck;
 };
 
 // RS_CTAS_PER_SM CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per CTA.
@@ -136,17 +142,28 @@ __device__ __forceinline__ bool regular_sum(float s) {
 // ---------------------------------------------------------------------------
 // Warp-cooperative exact serial sum: s_i = fl(s_{i-1} + a_i) over i < n,
 // starting from the exact value s.  Returns the first i with s_i > theta
-// (s = s_i), or n (s = s_{n-1}).  While s is a normal number well above
+// (s = s_i), or n (s = s_{n-1}).  With ck_s, the first 32 steps record
+// (element index, sum of the elements before it) in ck_pos / ck_s and their
+// count in *n_ck.  While s is a normal number well above
 // 2^-100, 32 addends are handled per step: each lane forms its addend's
 // chain function in the binade of s, an inclusive warp scan composes them,
 // and every lane whose running sum stays in that binade is exact; the addend
 // that leaves the binade is added for real.  Addends must be >= 0.
 // ---------------------------------------------------------------------------
 template <class Get>
-__device__ int warp_chain(const Get& get, int n, float& s, float theta) {
+__device__ int warp_chain(const Get& get, int n, float& s, float theta, float* ck_s = nullptr,
+                          int* ck_pos = nullptr, int* n_ck = nullptr) {
     const int lane = threadIdx.x & 31;
-    int pos = 0;
+    int pos = 0, nck = 0;
     while (pos < n) {
+        if (ck_s && nck < 32) {  // checkpoint: s is the sum of elements [0, pos)
+            if (lane == 0) {
+                ck_s[nck] = s;
+                ck_pos[nck] = pos;
+                *n_ck = nck + 1;
+            }
+            ++nck;
+        }
         const int i = pos + lane;
         const float x = (i < n) ? get(i) : 0.0f;
         if (regular_sum(s)) {
@@ -364,14 +381,17 @@ __device__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int
 // then cum_i), or n (cum = cum_{n-1}), over the chunk functions of
 // build_walk_fns (built for n0 >= n keys).  Whole segments and chunks are
 // applied while they stay in one binade and end at or below theta; the chunk
-// that crosses theta or a binade is walked element by element.
+// that crosses theta or a binade is walked element by element.  ck_s records
+// the sum before each segment walked; (seg0, s0) resumes at a recorded one.
 template <class Get>
-__device__ int walk_fns(const StreamSmem& sm, int n, float theta, float& cum, const Get& get) {
+__device__ int walk_fns(const StreamSmem& sm, int n, float theta, float& cum, const Get& get, float* ck_s = nullptr,
+                        int seg0 = 0, float s0 = 0.0f) {
     const int lane = threadIdx.x & 31;
-    float s = 0.0f;
+    float s = s0;
     const int nchk = (n + kSC - 1) / kSC;
     const int nseg = (nchk + 31) / 32;
-    for (int seg = 0; seg < nseg; ++seg) {
+    for (int seg = seg0; seg < nseg; ++seg) {
+        if (ck_s && lane == 0) ck_s[seg] = s;  // the sum of the elements before segment seg
         const int cnt = min(32, nchk - seg * 32);
         const float4 wf = sm.wfn[seg];
         const uint32_t wz = __float_as_uint(wf.z);
@@ -436,8 +456,9 @@ __device__ int walk_fns(const StreamSmem& sm, int n, float theta, float& cum, co
     return n;
 }
 
-__device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, int n, float theta, float& cum) {
-    return walk_fns(sm, n, theta, cum, [&](int i) { return key_prob(kb[i]); });
+__device__ int walk_chunks(const StreamSmem& sm, const unsigned long long* kb, int n, float theta, float& cum,
+                           float* ck_s = nullptr, int seg0 = 0, float s0 = 0.0f) {
+    return walk_fns(sm, n, theta, cum, [&](int i) { return key_prob(kb[i]); }, ck_s, seg0, s0);
 }
 
 // ---------------------------------------------------------------------------
@@ -1201,12 +1222,31 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                         auto get = [&](int i) { return key_prob(kb[i]); };
                         float cum = 0.0f;
                         // llama2.c:1036-1043
-                        int last = big ? walk_chunks(sm, kb, n0, topp, cum) : warp_chain(get, n0, cum, topp);
+                        int last = big ? walk_chunks(sm, kb, n0, topp, cum, sm.ck_s)
+                                       : warp_chain(get, n0, cum, topp, sm.ck_s, sm.ck_pos, &sm.n_ck);
                         if (last >= n0) last = all_cand ? n0 - 1 : -1;  // llama2.c:1037
                         if (last >= 0) {
                             const float r = __fmul_rn(coin, cum);  // llama2.c:1046
-                            float s3 = 0.0f;
-                            int k = big ? walk_chunks(sm, kb, last + 1, r, s3) : warp_chain(get, last + 1, s3, r);
+                            // llama2.c:1047-1054 adds the same p's in the same
+                            // order as the first walk, so it resumes at the
+                            // last checkpoint whose sum is <= r (no earlier
+                            // cdf can exceed r)
+                            __syncwarp();
+                            int k;
+                            if (big) {
+                                const int seg_last = last / (32 * kSC);
+                                const unsigned okm = __ballot_sync(kFullMask, lane <= seg_last && !(sm.ck_s[lane] > r));
+                                const int seg0 = 31 - __clz(okm);  // segment 0 (sum 0) always qualifies
+                                float s3 = 0.0f;
+                                k = walk_chunks(sm, kb, last + 1, r, s3, nullptr, seg0, sm.ck_s[seg0]);
+                            } else {
+                                const unsigned okm = __ballot_sync(
+                                    kFullMask, lane < sm.n_ck && sm.ck_pos[lane] <= last && !(sm.ck_s[lane] > r));
+                                const int q = 31 - __clz(okm);  // checkpoint 0 (pos 0, sum 0) always qualifies
+                                const int p0 = sm.ck_pos[q];
+                                float s3 = sm.ck_s[q];
+                                k = p0 + warp_chain([&](int i) { return key_prob(kb[p0 + i]); }, last + 1 - p0, s3, r);
+                            }
                             if (k > last) k = last;  // llama2.c:1055
                             res = key_index(kb[k]);
                         }
