@@ -444,7 +444,11 @@ def run_ours(args):
     ms = ev0.elapsed_time(ev1) / args.steps
     kernel_ms = float(np.mean([a.elapsed_time(b) for a, b in kev]))
     t = torch.tensor([ms, kernel_ms], dtype=torch.float64, device=dev)
+    rank_ms = [ms]
     if world > 1:
+        every = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(every, t)
+        rank_ms = [float(v[0]) for v in every]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, kernel_ms = float(t[0]), float(t[1])
 
@@ -491,7 +495,7 @@ def run_ours(args):
                     config=dict(workload=WORKLOAD, global_batch=world * B, rows_per_gpu=B, vocab=VOCAB,
                                 temperature=TEMP, parallelism=f"rows sharded over {world} GPU(s), no collective",
                                 l2="inputs 524 MB per GPU > 126 MB L2; no flush"),
-                    hbm_gbs=world * alg_bytes / (ms * 1e-3) / 1e9,
+                    hbm_gbs=world * alg_bytes / (ms * 1e-3) / 1e9, ms_per_step_by_rank=rank_ms,
                     roofline=dict(bound="hbm", achieved=achieved, peak=peak, unit="GB/s", frac=achieved / peak,
                                   traffic=traffic, kernel="row_stream_kernel", kernel_ms=kernel_ms,
                                   peak_source=peak_note),
