@@ -181,7 +181,9 @@ XM_HD bool chain_build(const float (&a)[N], uint32_t eb, ChainFn& f) {
     const float v0s = XM_U2F(eb << 23);
     const float v1s = XM_U2F((eb << 23) | 1u);
     float v0 = v0s, v1 = v1s;
+#if defined(__CUDA_ARCH__)
 #pragma unroll
+#endif
     for (int i = 0; i < N; ++i) {
         v0 = XM_ADD(v0, a[i]);
         v1 = XM_ADD(v1, a[i]);
