@@ -347,8 +347,23 @@ def run_decode(args):
                                      np.array([f["seed"]], np.uint64), nthreads=1)[0]
             return int(ids_r[0])
 
+        # the same step captured once in a CUDA graph and replayed (the
+        # library's buffers exist after the eager warm-up above)
+        for _ in range(3):
+            ours()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            pkg.seed_states(st, f["seed"])
+            pkg.classifier_sample_fused(h, w, temp, f["topp"], st, out_ids=ids)
+
+        def ours_graph():
+            graph.replay()
+            ids_host.copy_(ids)
+            return int(ids_host[0])
+
         res = {}
-        for name, fn in (("ours", ours), ("reference_path", reference)):
+        for name, fn in (("ours", ours), ("ours_graph", ours_graph), ("reference_path", reference)):
             for _ in range(max(args.warmup, 3)):
                 fn()
             torch.cuda.synchronize()
@@ -356,7 +371,10 @@ def run_decode(args):
             for _ in range(args.steps):
                 fn()
             res[name] = (time.perf_counter() - t0) / args.steps * 1e6
-        out["greedy" if temp == 0.0 else "topp"] = dict(ours_us=res["ours"], reference_path_us=res["reference_path"])
+        assert ours_graph() == ours()  # the replay samples what the eager call does
+        out["greedy" if temp == 0.0 else "topp"] = dict(ours_us=res["ours"], ours_graph_us=res["ours_graph"],
+                                                        reference_path_us=res["reference_path"])
+        del graph
     # the classifier alone (classifier_gemv_kernel at one row), device-timed on
     # its stream; W (262 MB) is larger than the 126 MB L2, so no flush
     stream = torch.cuda.current_stream()
