@@ -308,7 +308,22 @@ EDGE_CASES_FAST = EDGE + [
     ("tiny_logits", lambda r: np.random.default_rng(19).normal(0, 1e-30, (r, 32000)).astype(np.float32), 1.0, 0.9),
     ("some_tiny_logits", lambda r: _with(np.random.default_rng(20).normal(0, 2, (r, 32000)), list(range(0, 32000, 97)),
                                          1e-30), 0.7, 0.9),
+    # the eight largest logits of each row copied to two more places: short
+    # equal-p runs among the top candidates, ordered by index like glibc qsort
+    ("tied_candidates", lambda r: _tied_top(np.random.default_rng(21).normal(0, 2, (r, 32000)), 8, 2), 0.8, 0.9),
+    # temperatures outside [2^-10, 2^10]: rows the streaming kernel defers
+    ("tiny_temperature", lambda r: np.random.default_rng(22).normal(0, 1, (r, 32000)).astype(np.float32), 1e-4, 0.9),
+    ("huge_temperature", lambda r: np.random.default_rng(23).normal(0, 2, (r, 32000)).astype(np.float32), 3000.0, 0.9),
 ]
+
+
+def _tied_top(x, top, copies):
+    x = x.astype(np.float32)
+    rng = np.random.default_rng(24)
+    for row in x:
+        for j in np.argsort(row)[-top:]:
+            row[rng.choice(len(row), copies, replace=False)] = row[j]
+    return x
 
 
 def _with(x, cols, value):
