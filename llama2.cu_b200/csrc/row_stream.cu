@@ -54,17 +54,21 @@ namespace b2s {
 
 #define RS_THREADS 256
 #define RS_CTAS_PER_SM 4
+#define RS_SORT_GROUP 32
 #define RS_NS rs256
 #include "row_stream_impl.cuh"
 #undef RS_NS
+#undef RS_SORT_GROUP
 #undef RS_CTAS_PER_SM
 #undef RS_THREADS
 
 #define RS_THREADS 1024
 #define RS_CTAS_PER_SM 1
+#define RS_SORT_GROUP 8
 #define RS_NS rs1024
 #include "row_stream_impl.cuh"
 #undef RS_NS
+#undef RS_SORT_GROUP
 #undef RS_CTAS_PER_SM
 #undef RS_THREADS
 

@@ -1,7 +1,7 @@
 // row_stream_impl.cuh -- body of the streaming top-p kernel, included by
 // row_stream.cu once per CTA shape (RS_THREADS threads, RS_CTAS_PER_SM CTAs
-// per SM, in namespace b2s::RS_NS).  The algorithm is described in
-// row_stream.cu.
+// per SM, RS_SORT_GROUP bins per sort group, in namespace b2s::RS_NS).  The
+// algorithm is described in row_stream.cu.
 namespace RS_NS {
 namespace {
 
@@ -542,22 +542,29 @@ __device__ void build_cdf_fns(StreamSmem& sm, const Ctx& c, float S, const float
 }
 
 // Sorts every bin 0..D of the scattered nucleus by (e desc, index asc).  Warps
-// 1-7 take groups of 32 bins from a shared counter (warp 0 resolving S in the
-// meantime; having it join afterwards measured slower).  Bins of up to 16
-// keys: each key's rank is the number of
-// larger keys in its bin (keys are distinct); larger bins: bitonic networks.
-// Inside one bin (not the last) the value's top 15 bits are fixed, so 32-bit
-// keys (low 17 value bits, 0x7FFF - index) order them for V < 0x7FFF.
+// 1.. take groups of RS_SORT_GROUP bins from a shared counter (warp 0
+// resolving S in the meantime; having it join afterwards measured slower):
+// 32 bins with 4 CTAs per SM, where many rows share the SM; 8 bins with one
+// CTA per SM, where a single row's large nucleus would otherwise leave most
+// of its 31 warps without a group (15% faster there; 2% slower on the
+// 4-CTA shape's mostly small nuclei).  Bins of up to 16 keys: each key's rank
+// is the number of larger keys in its bin (keys are distinct); larger bins:
+// bitonic networks.  Inside one bin (not the last) the value's top 15 bits
+// are fixed, so 32-bit keys (low 17 value bits, 0x7FFF - index) order them
+// for V < 0x7FFF.
+constexpr int kSortGroup = RS_SORT_GROUP;  // bins per group taken by one warp (<= 32)
+static_assert(kSortGroup >= 1 && kSortGroup <= 32, "a warp sorts up to 32 bins at a time");
+
 __device__ void sort_bins(StreamSmem& sm, unsigned long long* kb, int D, int K, int V) {
     const int lane = threadIdx.x & 31;
     for (;;) {
         int g = 0;
         if (lane == 0) g = atomicAdd(&sm.sort_next, 1);
-        const int b0 = __shfl_sync(kFullMask, g, 0) * 32;
+        const int b0 = __shfl_sync(kFullMask, g, 0) * kSortGroup;
         if (b0 > D) break;
         const int b = b0 + lane;
         int s0 = 0, n = 0;
-        if (b <= D) {
+        if (lane < kSortGroup && b <= D) {
             s0 = sm.bstart[b];
             n = sm.hist[b] - s0;
             if (s0 < 0 || s0 + n > K || n > 256) sm.flag = 1;
