@@ -323,6 +323,7 @@ __device__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int
         float a = 0.0f;
         if (t < nchk) {
             const int cnt = min(kSC, n0 - kSC * t);
+#pragma unroll 8  // loads in flight from the L2 scratch
             for (int j = 0; j < cnt; ++j) a += key_prob(kb[kSC * t + j]);
         }
         sig[sidx] = a;
@@ -344,6 +345,7 @@ __device__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int
         const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
         const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
         float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
+#pragma unroll 8
         for (int j = 0; j < cnt; ++j) {
             const float x = key_prob(kb[kSC * t + j]);
             v0 = __fadd_rn(v0, x);
