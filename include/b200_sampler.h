@@ -68,6 +68,16 @@ int sample_topp(float* probabilities, int n, float topp, ProbIndex* probindex, f
  * reference.  Returns the token id (or -1 if the device call failed; see
  * sampler_last_error()). */
 int sample(Sampler* sampler, float* logits);
+/* Replaces sample_debug, llama2_cublas.cu:5067-5111 (the per-token call of
+ * that translation unit, :5905): sample() except that a `logits` buffer
+ * holding any NaN returns token 1 (no coin drawn, buffer left as it is) and
+ * any temperature below 1e-6f (zero and negative ones included) takes the
+ * argmax.  Its diagnostic printf lines are not reproduced. */
+int sample_debug(Sampler* sampler, float* logits);
+/* Replaces do_sample, llama2_cublas_fp16.cu:1178-1189 (static there; the same
+ * function is llama2_cublas_bf16.cu:1183 and llama2_cublas_fp16tc.cu:1222):
+ * sample() except that any temperature below 1e-6f takes the argmax. */
+int do_sample(Sampler* sampler, float* logits);
 
 /* ------------------------------------------------------------------------
  * Part 2: batched device API (no counterpart in the reference; it extends
@@ -92,6 +102,17 @@ int sample(Sampler* sampler, float* logits);
 /* Flags for SamplerBatchConfig.flags */
 #define SAMPLER_FLAG_PROBS_IN 1 /* rows are probabilities: skip /T and softmax, go straight to
                                    sample_mult / sample_topp (the coin is still drawn) */
+#define SAMPLER_FLAG_GREEDY_BELOW_1E6 2 /* a row whose temperature is below 1e-6f (zero and negative
+                                           ones included) takes the argmax, as do_sample
+                                           (llama2_cublas_fp16.cu:1179) and sample_debug
+                                           (llama2_cublas.cu:5089) decide; without the flag only
+                                           temperature == 0 does, as sample() (llama2.c:1085) */
+#define SAMPLER_FLAG_NAN_TOKEN1 4 /* a row holding any NaN logit gets token 1, draws no coin, leaves
+                                     probs_out as the logits and is flagged SAMPLER_ROW_NAN, as
+                                     sample_debug does (llama2_cublas.cu:5071-5085) */
+/* The per-row rules of the reference's two other per-token calls. */
+#define SAMPLER_MODE_DO_SAMPLE SAMPLER_FLAG_GREEDY_BELOW_1E6
+#define SAMPLER_MODE_SAMPLE_DEBUG (SAMPLER_FLAG_GREEDY_BELOW_1E6 | SAMPLER_FLAG_NAN_TOKEN1)
 
 /* Largest vocabulary the on-chip row path supports (the row is staged whole
  * in shared memory). */
@@ -101,7 +122,7 @@ typedef struct {
     int vocab_size;    /* V, 2 <= V <= SAMPLER_MAX_VOCAB */
     float temperature; /* used for every row unless temperature_rows != NULL */
     float topp;        /* used for every row unless topp_rows != NULL */
-    int flags;         /* SAMPLER_FLAG_* */
+    int flags;         /* SAMPLER_FLAG_* (PROBS_IN does not combine with the other two) */
 } SamplerBatchConfig;
 
 /* Bytes of device workspace sampler_batched needs for `batch` rows of
@@ -125,7 +146,9 @@ size_t sampler_workspace_bytes(int batch, int vocab_size);
  *   workspace        NULL (library-managed) or >= sampler_workspace_bytes()
  * Per row it follows sample() (llama2.c:1082-1105) exactly: greedy when
  * temperature == 0, else /T, softmax, coin, then sample_mult when topp <= 0
- * or topp >= 1, else sample_topp.  Asynchronous on `stream`. */
+ * or topp >= 1, else sample_topp (with SAMPLER_MODE_SAMPLE_DEBUG or
+ * SAMPLER_MODE_DO_SAMPLE in cfg->flags: sample_debug's or do_sample's rules
+ * instead).  Asynchronous on `stream`. */
 int sampler_batched(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
                     const float* temperature_rows, const float* topp_rows, const float* coins,
                     unsigned long long* rng_state, int* out_ids, float* probs_out, int* row_flags,
@@ -164,7 +187,7 @@ const char* sampler_last_error(void);
  * does on those logits (same ids, states and flags).
  *   hidden     bf16 [batch, dim] row-major (16-byte aligned), dim % 8 == 0
  *   wcls       bf16 [vocab_size, dim] row-major (16-byte aligned)
- *   cfg        vocab_size % 32 == 0, <= SAMPLER_MAX_VOCAB; flags must be 0
+ *   cfg        vocab_size % 32 == 0, <= SAMPLER_MAX_VOCAB; flags: no PROBS_IN
  *   logits_out fp32 [batch, vocab_size] or NULL (then library-managed)
  * Other arguments as in sampler_batched().  Asynchronous on `stream`.
  * The per-chunk statistics (and the logits when logits_out is NULL) live in

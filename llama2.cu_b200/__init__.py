@@ -13,13 +13,17 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libb200_sampler.so")
 
 SAMPLER_FLAG_PROBS_IN = 1
+SAMPLER_FLAG_GREEDY_BELOW_1E6 = 2
+SAMPLER_FLAG_NAN_TOKEN1 = 4
+MODE_DO_SAMPLE = SAMPLER_FLAG_GREEDY_BELOW_1E6
+MODE_SAMPLE_DEBUG = SAMPLER_FLAG_GREEDY_BELOW_1E6 | SAMPLER_FLAG_NAN_TOKEN1
 ROW_NAN, ROW_NO_CANDIDATE, ROW_SLOW_PATH, ROW_SERIAL, ROW_TIMEOUT = 1, 2, 4, 8, 16
 MAX_VOCAB = 32768
 
 # Every symbol the header declares (the CPU tests check the library exports them).
 EXPORTED_SYMBOLS = [
     "build_sampler", "free_sampler", "random_u32", "random_f32", "sample_argmax", "sample_mult",
-    "sample_topp", "sample", "sampler_workspace_bytes", "sampler_batched", "sampler_batched_host",
+    "sample_topp", "sample", "sample_debug", "do_sample", "sampler_workspace_bytes", "sampler_batched", "sampler_batched_host",
     "sampler_seed_states", "sampler_last_launch_count", "sampler_last_error", "sampler_shard_rows",
     "sampler_nccl_get_unique_id", "sampler_nccl_comm_init", "sampler_nccl_allgather_ids",
     "sampler_nccl_comm_destroy", "sampler_batched_noalloc", "classifier_sample_fused",
@@ -80,6 +84,10 @@ def lib():
     L.sample_topp.restype = c_int
     L.sample.argtypes = [ctypes.POINTER(Sampler), fp]
     L.sample.restype = c_int
+    L.sample_debug.argtypes = [ctypes.POINTER(Sampler), fp]
+    L.sample_debug.restype = c_int
+    L.do_sample.argtypes = [ctypes.POINTER(Sampler), fp]
+    L.do_sample.restype = c_int
     L.sampler_workspace_bytes.argtypes = [c_int, c_int]
     L.sampler_workspace_bytes.restype = c_size
     L.sampler_batched.argtypes = [ctypes.POINTER(SamplerBatchConfig), P, c_int, ctypes.c_longlong, P, P, P,
@@ -156,10 +164,11 @@ def _stream_ptr(stream):
 
 def sample_batched(logits, temperature, topp, rng_state=None, *, temperature_rows=None, topp_rows=None,
                    coins=None, out_ids=None, probs_out=None, row_flags=None, probs_in=False,
-                   workspace=None, stream=None):
+                   workspace=None, stream=None, mode=0):
     """Batched device sampling over the rows of a CUDA fp32 tensor [B, ld].
 
     rng_state: int64 CUDA tensor [B] advanced in place (uint64 bit patterns).
+    mode: 0 (sample()'s rules), MODE_SAMPLE_DEBUG or MODE_DO_SAMPLE.
     Returns out_ids (int32 CUDA tensor [B]).  Asynchronous on `stream`.
     """
     import torch
@@ -169,7 +178,7 @@ def sample_batched(logits, temperature, topp, rng_state=None, *, temperature_row
     B, V = logits.shape
     if out_ids is None:
         out_ids = torch.empty(B, dtype=torch.int32, device=logits.device)
-    cfg = SamplerBatchConfig(V, float(temperature), float(topp), SAMPLER_FLAG_PROBS_IN if probs_in else 0)
+    cfg = SamplerBatchConfig(V, float(temperature), float(topp), (SAMPLER_FLAG_PROBS_IN if probs_in else 0) | mode)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     rc = lib().sampler_batched(ctypes.byref(cfg), _ptr(logits), B, logits.stride(0), _ptr(temperature_rows),
                                _ptr(topp_rows), _ptr(coins), _ptr(rng_state), _ptr(out_ids), _ptr(probs_out),
@@ -297,11 +306,12 @@ def free_sampler(s):
     lib().free_sampler(ctypes.byref(s))
 
 
-def sample(s, logits_np):
+def sample(s, logits_np, entry="sample"):
     """llama2.c sample(): logits_np (float32, writable) is overwritten with the
-    probabilities when temperature != 0."""
+    probabilities when temperature != 0.  entry="sample_debug" / "do_sample"
+    calls the variants of the reference's CUDA translation units instead."""
     fp = logits_np.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
-    r = lib().sample(ctypes.byref(s), fp)
+    r = getattr(lib(), entry)(ctypes.byref(s), fp)
     if r < 0:
-        raise SamplerError("sample failed: " + lib().sampler_last_error().decode())
+        raise SamplerError(f"{entry} failed: " + lib().sampler_last_error().decode())
     return r

@@ -69,8 +69,13 @@ extern "C" int sampler_batched_noalloc(const SamplerBatchConfig* cfg, const floa
     if (batch < 0 || V < 1 || ld < V) return SAMPLER_E_INVALID;
     if (V > SAMPLER_NOALLOC_MAX_VOCAB) return SAMPLER_E_UNSUPPORTED;
     if (batch == 0) return SAMPLER_OK;
+    const int mode_bits = SAMPLER_FLAG_GREEDY_BELOW_1E6 | SAMPLER_FLAG_NAN_TOKEN1;
+    if (cfg->flags & ~(SAMPLER_FLAG_PROBS_IN | mode_bits)) return SAMPLER_E_INVALID;
     const bool probs_in = (cfg->flags & SAMPLER_FLAG_PROBS_IN) != 0;
-    const bool any_draw = probs_in || temperature_rows || cfg->temperature != 0.0f;
+    if (probs_in && (cfg->flags & mode_bits)) return SAMPLER_E_INVALID;
+    const bool greedy_eps = (cfg->flags & SAMPLER_FLAG_GREEDY_BELOW_1E6) != 0;
+    const bool any_draw = probs_in || temperature_rows ||
+                          !(cfg->temperature == 0.0f || (greedy_eps && cfg->temperature < 1e-6f));
     if (any_draw && !coins && !rng_state) return SAMPLER_E_INVALID;
 
     int dev = 0;
@@ -104,6 +109,8 @@ extern "C" int sampler_batched_noalloc(const SamplerBatchConfig* cfg, const floa
     p.ws_stride = (long long)stride;
     p.probs_in = probs_in ? 1 : 0;
     p.force_mode = 0;
+    p.greedy_eps = greedy_eps ? 1 : 0;
+    p.nan_token1 = (cfg->flags & SAMPLER_FLAG_NAN_TOKEN1) ? 1 : 0;
     const int n = b2s::launch_row_sampler(p, ctas, (cudaStream_t)stream);
     return n < 0 ? SAMPLER_E_CUDA : SAMPLER_OK;
 }

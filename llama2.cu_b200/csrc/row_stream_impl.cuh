@@ -724,7 +724,9 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
         c.nch = nch;
         c.T = p.temperature_rows ? p.temperature_rows[row] : p.temperature;
         const float topp = p.topp_rows ? p.topp_rows[row] : p.topp;
-        const bool greedy = (c.T == 0.0f);
+        // sample(): T == 0 (llama2.c:1085); do_sample / sample_debug: T < 1e-6f
+        // (llama2_cublas_fp16.cu:1179, llama2_cublas.cu:5089)
+        const bool greedy = (c.T == 0.0f) || (p.greedy_eps && c.T < 1e-6f);
         // sample_mult rows (topp outside (0, 1), llama2.c:1098-1100) share the
         // passes and take the cdf walk at the end
         const bool mult = !greedy && (topp <= 0.0f || topp >= 1.0f);
@@ -733,12 +735,17 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
             // first index of the strict max, NaN at index 0 wins (llama2.c:981-992)
             float bv = -INFINITY;
             int bi = 0x7FFFFFFF;
+            bool has_nan = false;
             for (int sidx = 0; sidx < kStrips; ++sidx) {
                 const int t = sidx * kST + tid;
                 if (t >= nch) break;
                 float a[kSC];
                 load_chunk(c, t, a);
                 const int cnt = min(kSC, V - t * kSC);
+                if (p.nan_token1) {  // sample_debug's NaN test (padding lanes are 0)
+#pragma unroll
+                    for (int j = 0; j < kSC; ++j) has_nan |= isnan(a[j]);
+                }
                 if (p.probs_out) {  // sample() leaves the logits in place when greedy
                     float4* dst = reinterpret_cast<float4*>(p.probs_out + (long long)row * V + t * kSC);
 #pragma unroll
@@ -765,15 +772,16 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 sm.red_a[warp] = bv;
                 sm.red_i[warp] = bi;
             }
-            __syncthreads();
+            const bool nan1 = __syncthreads_or(has_nan) != 0;
             if (tid == 0) {
                 for (int w = 1; w < kSW; ++w)
                     if (sm.red_a[w] > bv || (sm.red_a[w] == bv && sm.red_i[w] < bi)) {
                         bv = sm.red_a[w];
                         bi = sm.red_i[w];
                     }
-                p.out_ids[row] = (isnan(__ldg(c.src)) || bi == 0x7FFFFFFF) ? 0 : bi;
-                if (p.row_flags) p.row_flags[row] = 0;
+                // a NaN row under sample_debug's rule is token 1 (llama2_cublas.cu:5081-5084)
+                p.out_ids[row] = nan1 ? 1 : ((isnan(__ldg(c.src)) || bi == 0x7FFFFFFF) ? 0 : bi);
+                if (p.row_flags) p.row_flags[row] = nan1 ? kFlagNan : 0;
             }
             __syncthreads();
             continue;
@@ -785,6 +793,7 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
         const float k2 = c.rT * 1.4426950408889634f;  // log2(e)/T, approximate scale
         float mxl = -INFINITY, mnl = INFINITY, M2loc = -3.4e38f;
         float cm2[kStrips], cs2[kStrips];
+        bool has_nan = false;  // any NaN logit, tested only under sample_debug's rule
         const float4* stats = p.stats ? p.stats + (long long)row * p.stats_ld : nullptr;
 #pragma unroll
         for (int sidx = 0; sidx < kStrips; ++sidx) {
@@ -792,6 +801,12 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
             float m2 = -3.4e38f, s2 = 0.0f;
             if (stats) {
                 // the same quantities from the classifier GEMM epilogue
+                if (p.nan_token1 && t < nch) {
+                    float a[kSC];
+                    load_chunk(c, t, a);
+#pragma unroll
+                    for (int j = 0; j < kSC; ++j) has_nan |= isnan(a[j]);
+                }
                 if (t < nch) {
                     const float4 q = stats[t];
                     mxl = fmaxf(mxl, q.x);
@@ -803,6 +818,10 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 float a[kSC];
                 load_chunk(c, t, a);  // eight loads in flight
                 const int cnt = min(kSC, V - t * kSC);
+                if (p.nan_token1) {
+#pragma unroll
+                    for (int j = 0; j < kSC; ++j) has_nan |= isnan(a[j]);
+                }
                 if (cnt == kSC) {
                     // max of fl(a*k2) is fl(max(a)*k2) for k2 > 0 (rounding is
                     // monotone), fl(min(a)*k2) for k2 < 0
@@ -862,7 +881,21 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
             MN = fminf(MN, sm.red_b[w]);
             M2 = fmaxf(M2, sm.red_c[w]);
         }
-        __syncthreads();  // red_* are reused by the scans below
+        // red_* are reused by the scans below
+        if (__syncthreads_or(has_nan)) {
+            // sample_debug (llama2_cublas.cu:5071-5085): token 1, no coin, the
+            // buffer keeps the logits
+            if (p.probs_out) {
+                const float4* src4 = reinterpret_cast<const float4*>(c.src);
+                float4* dst4 = reinterpret_cast<float4*>(p.probs_out + (long long)row * V);
+                for (int g = tid; g < V / 4; g += kST) dst4[g] = __ldg(src4 + g);
+            }
+            if (tid == 0) {
+                p.out_ids[row] = 1;
+                if (p.row_flags) p.row_flags[row] = kFlagNan;
+            }
+            continue;
+        }
         c.max_x = c.unit ? MX : (c.T > 0.0f ? __fdiv_rn(MX, c.T) : __fdiv_rn(MN, c.T));
         // Rows this kernel takes: x = l/T by the unguarded Markstein division,
         // correctly rounded for |T| in [2^-10, 2^10] and |l| in [2^-60, 2^60]

@@ -49,6 +49,20 @@ size_t next_pow2(size_t x) {
     return p;
 }
 
+// Library-managed buffers of one (device, stream): calls on different
+// streams never share scratch, so they may overlap on the GPU.
+struct StreamBufs {
+    cudaStream_t stream = nullptr;
+    unsigned long long* workspace = nullptr;  // sampler_batched with workspace == NULL
+    size_t workspace_bytes = 0;
+    float* flogits = nullptr;  // fused classifier: logits when the caller passes none
+    size_t flogits_cap = 0;
+    float4* stats = nullptr;   // fused classifier: per-chunk statistics
+    size_t stats_cap = 0;
+    void* hnorm = nullptr;     // bf16 normalized hidden states
+    size_t hnorm_cap = 0;
+};
+
 // Per-device state for the library-managed buffers.
 struct DeviceCtx {
     // Serializes the host-buffer entry points on this device: they share the
@@ -60,28 +74,26 @@ struct DeviceCtx {
     cudaStream_t stream = nullptr;   // used by the single-row llama2.c entry points
     cudaStream_t streams[2] = {nullptr, nullptr};  // host-buffer pipeline
     int* error_word = nullptr;
-    unsigned long long* workspace = nullptr;
-    size_t workspace_bytes = 0;
-    // single-row buffers
+    // single-row buffers (the llama2.c entry points, serialized by host_mu)
+    unsigned long long* host_ws = nullptr;
+    size_t host_ws_bytes = 0;
     float* d_row = nullptr;
     float* d_probs = nullptr;
     float* d_coin = nullptr;
+    unsigned long long* d_state1 = nullptr;  // the Sampler's state when the device draws
     int* d_id = nullptr;
     int row_cap = 0;
-    // host-pipeline buffers
+    // host-pipeline buffers (sampler_batched_host, serialized by host_mu)
+    unsigned long long* pipe_ws = nullptr;
+    size_t pipe_ws_bytes = 0;
     float* d_logits = nullptr;
     size_t logits_cap = 0;
     float* d_topp = nullptr;
     unsigned long long* d_state = nullptr;
     int* d_ids = nullptr;
     int rows_cap = 0;
-    // fused classifier: logits and per-chunk statistics
-    float* d_flogits = nullptr;
-    size_t flogits_cap = 0;
-    float4* d_stats = nullptr;
-    size_t stats_cap = 0;
-    void* d_hnorm = nullptr;  // bf16 normalized hidden states
-    size_t hnorm_cap = 0;
+    // per-stream buffers, created on a stream's first call and kept until exit
+    std::vector<StreamBufs*> per_stream;
 };
 
 std::mutex g_mu;
@@ -103,20 +115,34 @@ int get_ctx(DeviceCtx** out) {
         B2S_CUDA(cudaMemset(c->error_word, 0, sizeof(int)));
         B2S_CUDA(cudaMalloc(&c->d_coin, 4 * sizeof(float)));
         B2S_CUDA(cudaMalloc(&c->d_id, 4 * sizeof(int)));
+        B2S_CUDA(cudaMalloc(&c->d_state1, sizeof(unsigned long long)));
         g_ctx[dev] = c;
     }
     *out = g_ctx[dev];
     return SAMPLER_OK;
 }
 
-int ensure_workspace(DeviceCtx* c, size_t bytes) {
-    if (c->workspace_bytes >= bytes) return SAMPLER_OK;
-    if (c->workspace) cudaFree(c->workspace);
-    c->workspace = nullptr;
-    c->workspace_bytes = 0;
-    B2S_CUDA(cudaMalloc(&c->workspace, bytes));
-    c->workspace_bytes = bytes;
+// Grows a library-managed buffer to at least `bytes` (callers hold g_mu).
+// cudaFree waits for the device, so work still using the old buffer ends first.
+template <class T>
+int ensure_buf(T** ptr, size_t* cap, size_t bytes) {
+    if (*cap >= bytes) return SAMPLER_OK;
+    if (*ptr) cudaFree(*ptr);
+    *ptr = nullptr;
+    *cap = 0;
+    B2S_CUDA(cudaMalloc(reinterpret_cast<void**>(ptr), bytes));
+    *cap = bytes;
     return SAMPLER_OK;
+}
+
+// The buffers of `stream` on device context c (callers hold g_mu).
+StreamBufs* stream_bufs(DeviceCtx* c, cudaStream_t stream) {
+    for (StreamBufs* b : c->per_stream)
+        if (b->stream == stream) return b;
+    StreamBufs* b = new StreamBufs();
+    b->stream = stream;
+    c->per_stream.push_back(b);
+    return b;
 }
 
 int ensure_row(DeviceCtx* c, int V) {
@@ -170,9 +196,20 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
     if (V > SAMPLER_MAX_VOCAB)
         return fail(SAMPLER_E_UNSUPPORTED, "vocab_size %d above SAMPLER_MAX_VOCAB %d", V, SAMPLER_MAX_VOCAB);
     if (batch == 0) return SAMPLER_OK;
+    const int mode_bits = SAMPLER_FLAG_GREEDY_BELOW_1E6 | SAMPLER_FLAG_NAN_TOKEN1;
+    if (cfg->flags & ~(SAMPLER_FLAG_PROBS_IN | mode_bits))
+        return fail(SAMPLER_E_INVALID, "unknown bits in flags 0x%x", cfg->flags);
     const bool probs_in = (cfg->flags & SAMPLER_FLAG_PROBS_IN) != 0;
-    const bool all_greedy = !probs_in && !temperature_rows && cfg->temperature == 0.0f && force_mode == 0;
-    if (!all_greedy && !coins && !rng_state)
+    if (probs_in && (cfg->flags & mode_bits))
+        return fail(SAMPLER_E_INVALID, "PROBS_IN does not combine with GREEDY_BELOW_1E6 / NAN_TOKEN1");
+    const bool greedy_eps = (cfg->flags & SAMPLER_FLAG_GREEDY_BELOW_1E6) != 0;
+    const bool nan_token1 = (cfg->flags & SAMPLER_FLAG_NAN_TOKEN1) != 0;
+    // every row greedy: one temperature for the batch at which the row rule takes the argmax
+    const bool uniform_greedy = !probs_in && !temperature_rows && force_mode == 0 &&
+                                (cfg->temperature == 0.0f || (greedy_eps && cfg->temperature < 1e-6f));
+    // the argmax kernel has no NaN test: under NAN_TOKEN1 the row kernels take greedy rows too
+    const bool all_greedy = uniform_greedy && !nan_token1;
+    if (!uniform_greedy && !coins && !rng_state)
         return fail(SAMPLER_E_INVALID, "rng_state is NULL but rows need a coin");
     DeviceCtx* c = nullptr;
     int rc = get_ctx(&c);
@@ -197,9 +234,10 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
         ws = static_cast<unsigned long long*>(workspace);
     } else {
         std::lock_guard<std::mutex> lk(g_mu);
-        rc = ensure_workspace(c, need);
+        StreamBufs* b = stream_bufs(c, stream);
+        rc = ensure_buf(&b->workspace, &b->workspace_bytes, need);
         if (rc) return rc;
-        ws = c->workspace;
+        ws = b->workspace;
     }
     char* wsb = reinterpret_cast<char*>(ws);
     int* defer_count = reinterpret_cast<int*>(wsb);
@@ -225,6 +263,8 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
     p.ws_stride = (long long)next_pow2((size_t)V);
     p.probs_in = probs_in ? 1 : 0;
     p.force_mode = force_mode;
+    p.greedy_eps = greedy_eps ? 1 : 0;
+    p.nan_token1 = nan_token1 ? 1 : 0;
     p.error_word = c->error_word;
     p.defer_count = defer_count;
     p.defer_rows = defer_rows;
@@ -266,9 +306,12 @@ int check_device_word(DeviceCtx* c) {
 }
 
 // One host row through the device: the shared body of the llama2.c
-// single-row entry points.  Returns the id or -1.
+// single-row entry points.  Returns the id or -1.  With `state` (a host
+// Sampler state) the device draws the coin when the row rule needs one and
+// the state comes back advanced or not, as the reference leaves it;
+// `mode_flags` are SAMPLER_FLAG_GREEDY_BELOW_1E6 / SAMPLER_FLAG_NAN_TOKEN1.
 int host_row(float* row, int n, float temperature, float topp, const float* coin, int probs_in,
-             int force_mode, bool write_back) {
+             int force_mode, bool write_back, unsigned long long* state = nullptr, int mode_flags = 0) {
     DeviceCtx* c = nullptr;
     if (get_ctx(&c)) return -1;
     std::lock_guard<std::mutex> host_lock(c->host_mu);
@@ -277,6 +320,10 @@ int host_row(float* row, int n, float temperature, float topp, const float* coin
         return -1;
     }
     if (ensure_row(c, n)) return -1;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (ensure_buf(&c->host_ws, &c->host_ws_bytes, workspace_for(c, n, 1))) return -1;
+    }
     cudaStream_t s = c->stream;
     if (cudaMemcpyAsync(c->d_row, row, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess) {
         fail(SAMPLER_E_CUDA, "H2D copy failed");
@@ -286,16 +333,25 @@ int host_row(float* row, int n, float temperature, float topp, const float* coin
         fail(SAMPLER_E_CUDA, "H2D coin copy failed");
         return -1;
     }
-    SamplerBatchConfig cfg{n, temperature, topp, probs_in ? SAMPLER_FLAG_PROBS_IN : 0};
+    if (state && cudaMemcpyAsync(c->d_state1, state, sizeof(*state), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        fail(SAMPLER_E_CUDA, "H2D state copy failed");
+        return -1;
+    }
+    SamplerBatchConfig cfg{n, temperature, topp, (probs_in ? SAMPLER_FLAG_PROBS_IN : 0) | mode_flags};
     // one row with its probabilities: the general kernel's single pass is the
     // lower latency here
-    const int rc = dispatch(&cfg, c->d_row, 1, n, nullptr, nullptr, coin ? c->d_coin : nullptr, nullptr, c->d_id,
-                            write_back ? c->d_probs : nullptr, nullptr, nullptr, 0, s, force_mode, nullptr, 0,
-                            !write_back);
+    const int rc = dispatch(&cfg, c->d_row, 1, n, nullptr, nullptr, coin ? c->d_coin : nullptr,
+                            state ? c->d_state1 : nullptr, c->d_id, write_back ? c->d_probs : nullptr, nullptr,
+                            c->host_ws, c->host_ws_bytes, s, force_mode, nullptr, 0, !write_back);
     if (rc) return -1;
     int id = -1;
     if (cudaMemcpyAsync(&id, c->d_id, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
         fail(SAMPLER_E_CUDA, "D2H id copy failed");
+        return -1;
+    }
+    unsigned long long st_back = 0;
+    if (state && cudaMemcpyAsync(&st_back, c->d_state1, sizeof(st_back), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+        fail(SAMPLER_E_CUDA, "D2H state copy failed");
         return -1;
     }
     if (write_back &&
@@ -308,6 +364,7 @@ int host_row(float* row, int n, float temperature, float topp, const float* coin
         return -1;
     }
     if (check_device_word(c)) return -1;
+    if (state) *state = st_back;
     return id;
 }
 
@@ -382,6 +439,23 @@ unsigned int random_u32(unsigned long long* state) {
 
 float random_f32(unsigned long long* state) { return (random_u32(state) >> 8) / 16777216.0f; }
 
+int sample_debug(Sampler* sampler, float* logits) {
+    // Whether the coin is drawn depends on the NaN test, so the device draws
+    // it from a copy of the state (llama2_cublas.cu:5071-5100).  A greedy
+    // row (T < 1e-6f) and a NaN row leave the buffer as it is.
+    const bool greedy = sampler->temperature < 1e-6f;
+    return host_row(logits, sampler->vocab_size, sampler->temperature, sampler->topp, nullptr, 0, 0, !greedy,
+                    &sampler->rng_state, SAMPLER_MODE_SAMPLE_DEBUG);
+}
+
+int do_sample(Sampler* sampler, float* logits) {
+    // llama2_cublas_fp16.cu:1179: any temperature below 1e-6f is greedy
+    if (sampler->temperature < 1e-6f)
+        return host_row(logits, sampler->vocab_size, 0.0f, sampler->topp, nullptr, 0, 0, false);
+    const float coin = random_f32(&sampler->rng_state);
+    return host_row(logits, sampler->vocab_size, sampler->temperature, sampler->topp, &coin, 0, 0, true);
+}
+
 int sample_argmax(float* probabilities, int n) {
     return host_row(probabilities, n, 0.0f, 0.0f, nullptr, 0, 0, false);
 }
@@ -449,22 +523,15 @@ int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, c
     float4* stats = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
-        if (!logits && c->flogits_cap < nlog) {
-            if (c->d_flogits) cudaFree(c->d_flogits);
-            c->d_flogits = nullptr;
-            c->flogits_cap = 0;
-            B2S_CUDA(cudaMalloc(&c->d_flogits, nlog * sizeof(float)));
-            c->flogits_cap = nlog;
+        StreamBufs* b = stream_bufs(c, (cudaStream_t)stream);
+        if (!logits) {
+            rc = ensure_buf(&b->flogits, &b->flogits_cap, nlog * sizeof(float));
+            if (rc) return rc;
+            logits = b->flogits;
         }
-        if (c->stats_cap < nst) {
-            if (c->d_stats) cudaFree(c->d_stats);
-            c->d_stats = nullptr;
-            c->stats_cap = 0;
-            B2S_CUDA(cudaMalloc(&c->d_stats, nst * sizeof(float4)));
-            c->stats_cap = nst;
-        }
-        if (!logits) logits = c->d_flogits;
-        stats = c->d_stats;
+        rc = ensure_buf(&b->stats, &b->stats_cap, nst * sizeof(float4));
+        if (rc) return rc;
+        stats = b->stats;
     }
     b2s::GemmLaunch g{};
     g.h = hidden;
@@ -516,14 +583,10 @@ int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* 
     void* h = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
-        if (c->hnorm_cap < need) {
-            if (c->d_hnorm) cudaFree(c->d_hnorm);
-            c->d_hnorm = nullptr;
-            c->hnorm_cap = 0;
-            B2S_CUDA(cudaMalloc(&c->d_hnorm, need));
-            c->hnorm_cap = need;
-        }
-        h = c->d_hnorm;
+        StreamBufs* b = stream_bufs(c, (cudaStream_t)stream);
+        rc = ensure_buf(&b->hnorm, &b->hnorm_cap, need);
+        if (rc) return rc;
+        h = b->hnorm;
     }
     const int n = b2s::launch_rmsnorm_bf16(x, norm_weight, batch, dim, h, (cudaStream_t)stream);
     if (n < 0) return fail(SAMPLER_E_CUDA, "rmsnorm launch: %s", cudaGetErrorString((cudaError_t)(-n)));
@@ -589,7 +652,9 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
     int rc = get_ctx(&c);
     if (rc) return rc;
     std::lock_guard<std::mutex> host_lock(c->host_mu);
-    const bool all_greedy = !(cfg->flags & SAMPLER_FLAG_PROBS_IN) && cfg->temperature == 0.0f;
+    const bool all_greedy = !(cfg->flags & SAMPLER_FLAG_PROBS_IN) &&
+                            (cfg->temperature == 0.0f ||
+                             ((cfg->flags & SAMPLER_FLAG_GREEDY_BELOW_1E6) && cfg->temperature < 1e-6f));
     if (!all_greedy && !rng_state) return fail(SAMPLER_E_INVALID, "rng_state is NULL");
     // Each of the two pipeline streams gets its own half of the workspace so
     // two chunks in flight never share slow-path scratch.
@@ -598,7 +663,7 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
     const size_t ws_half = (workspace_for(c, V, chunk) + 255) & ~(size_t)255;
     {
         std::lock_guard<std::mutex> lk(g_mu);
-        rc = ensure_workspace(c, 2 * ws_half);
+        rc = ensure_buf(&c->pipe_ws, &c->pipe_ws_bytes, 2 * ws_half);
         if (rc) return rc;
         const size_t need = (size_t)batch * (size_t)V;
         if (c->logits_cap < need) {
@@ -642,7 +707,7 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
         if (!all_greedy)
             B2S_CUDA(cudaMemcpyAsync(c->d_state + r0, rng_state + r0, rows * sizeof(unsigned long long),
                                      cudaMemcpyHostToDevice, s));
-        void* ws = reinterpret_cast<char*>(c->workspace) + (size_t)(k & 1) * ws_half;
+        void* ws = reinterpret_cast<char*>(c->pipe_ws) + (size_t)(k & 1) * ws_half;
         rc = dispatch(cfg, dl, rows, V, nullptr, topp_rows ? c->d_topp + r0 : nullptr, nullptr,
                       all_greedy ? nullptr : c->d_state + r0, c->d_ids + r0, nullptr, nullptr, ws, ws_half, s, 0);
         if (rc) return rc;

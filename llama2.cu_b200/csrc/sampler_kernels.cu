@@ -856,10 +856,25 @@ __global__ void __launch_bounds__(kRowThreads, 1) row_sampler_kernel(RowLaunch p
         c.probs_in = p.probs_in != 0;
         c.write_probs = p.probs_out != nullptr;
         c.probs_row = p.probs_out ? p.probs_out + (long long)row * V : nullptr;
-        const bool greedy = !c.probs_in && (c.T == 0.0f);
+        // sample(): T == 0 (llama2.c:1085); do_sample / sample_debug: T < 1e-6f
+        // (llama2_cublas_fp16.cu:1179, llama2_cublas.cu:5089)
+        const bool greedy = !c.probs_in && (c.T == 0.0f || (p.greedy_eps && c.T < 1e-6f));
+        // sample_debug's NaN test on the raw logits (llama2_cublas.cu:5071-5085)
+        bool nan1 = false;
+        if (p.nan_token1) {
+            bool h = false;
+            for (int i = tid; i < V; i += blockDim.x) h |= isnan(sm.row[i]);
+            nan1 = __syncthreads_or(h) != 0;
+        }
 
         int id = 0;
-        if (greedy) {
+        if (nan1) {
+            // token 1, no coin drawn, the buffer keeps the logits
+            id = 1;
+            flags |= kFlagNan;
+            if (c.write_probs)
+                for (int i = tid; i < V; i += blockDim.x) c.probs_row[i] = sm.row[i];
+        } else if (greedy) {
             id = row_argmax(sm, V);
             if (c.write_probs)
                 for (int i = tid; i < V; i += blockDim.x) c.probs_row[i] = sm.row[i];

@@ -29,6 +29,8 @@ struct RowLaunch {
     long long ws_stride;          // u64 entries per CTA (power of two >= vocab)
     int probs_in;                 // rows are probabilities
     int force_mode;               // 0: by topp as sample() does, 1: sample_mult, 2: sample_topp
+    int greedy_eps;               // rows with temperature < 1e-6f are greedy (do_sample, sample_debug)
+    int nan_token1;               // rows holding a NaN logit give token 1, no draw (sample_debug)
     int* error_word;              // device word, set on bounded-wait timeout
     // deferred rows: the streaming kernel appends rows it leaves to the
     // general kernel; the general kernel then walks row_list[0..*row_count)

@@ -14,7 +14,11 @@ workloads).
   topp         B=4096, seed 3: Gumbel(0, 1) noise plus a Zipf(s=1.1) ranked
                bonus A_r * k^-1.1 (k = 1..V over a per-row random
                permutation, A_r ~ U[0, 12] nats), T=0.7, topp 0.9 (even rows)
-               / 0.95 (odd rows), per-row state 42 + row.
+               / 0.95 (odd rows), per-row state 42 + row.  Row r has its own
+               generator, SeedSequence(3, spawn_key=(r,)), so any range of
+               global rows (a rank's shard of a multi-GPU batch) is drawn
+               without drawing the rows before it.  Nucleus sizes of the first
+               4096 rows span 1 to about 2400 tokens (tests/golden/topp.json).
   fused        hidden [8192, 4096] bf16 ~ N(0, 1), seed 4; wcls [32000, 4096]
                bf16 ~ N(0, 0.02^2); T=0.8, topp=0.9.
 """
@@ -48,19 +52,33 @@ def mult(rows=1024, vocab=VOCAB):
     return dict(logits=x, temperature=0.8, topp=1.0, seed=42)
 
 
-def topp(rows=4096, vocab=VOCAB):
-    rng = np.random.default_rng(3)
+def topp(rows=4096, vocab=VOCAB, first=0):
+    """Global rows [first, first + rows) of the top-p workload."""
     x = np.empty((rows, vocab), dtype=np.float32)
     ranks = np.arange(1, vocab + 1, dtype=np.float64) ** -1.1
-    for r in range(rows):
+    for i in range(rows):
+        rng = np.random.default_rng(np.random.SeedSequence(3, spawn_key=(first + i,)))
         g = rng.gumbel(0.0, 1.0, size=vocab)
         a = rng.uniform(0.0, 12.0)
         perm = rng.permutation(vocab)
         bonus = np.empty(vocab, dtype=np.float64)
         bonus[perm] = a * ranks
-        x[r] = (g + bonus).astype(np.float32)
-    topp_rows = np.where(np.arange(rows) % 2 == 0, 0.9, 0.95).astype(np.float32)
+        x[i] = (g + bonus).astype(np.float32)
+    topp_rows = np.where((first + np.arange(rows)) % 2 == 0, 0.9, 0.95).astype(np.float32)
     return dict(logits=x, temperature=0.7, topp=0.9, topp_rows=topp_rows, seed=42)
+
+
+def debug_rows(rows=64, vocab=VOCAB):
+    """Rows for the sample_debug / do_sample rules: N(0, 2^2) from seed 5,
+    with NaN planted in every seventh row (one position; all positions in
+    row 21)."""
+    rng = np.random.default_rng(5)
+    x = rng.normal(0.0, 2.0, size=(rows, vocab)).astype(np.float32)
+    for r in range(0, rows, 7):
+        x[r, int(rng.integers(vocab))] = np.nan
+    if rows > 21:
+        x[21, :] = np.nan
+    return dict(logits=x, temperatures=[0.8, 5e-7, 1e-6, 0.0, -0.5], topps=[0.9, 1.0], seed=42)
 
 
 def fused(rows=8192, dim=DIM, vocab=VOCAB):

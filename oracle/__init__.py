@@ -15,16 +15,20 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_sampler.so")
-REF_SOURCE_DIR = "/root/reference"
 
 
 def build(with_ref=True):
-    """Builds liboracle.so and, when the reference tree is present,
-    _ref/libref_sampler.so (uses oracle/Makefile)."""
-    targets = ["liboracle.so"]
-    if with_ref and os.path.isdir(REF_SOURCE_DIR):
-        targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
+    """Builds liboracle.so and, when the reference sources are reachable
+    (oracle/Makefile's REF_DIR, or the REFERENCE_DIR environment variable),
+    _ref/libref_sampler.so.  Where they are absent (the GPU box) the prebuilt
+    _ref library is used as it is."""
+    subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
+    if with_ref:
+        r = subprocess.run(["make", "-s", "-C", HERE, "ref"], stdout=subprocess.DEVNULL,
+                           stderr=subprocess.DEVNULL)
+        if r.returncode != 0 and not os.path.exists(REF_SO):
+            return False
+    return True
 
 
 _P = ctypes.c_void_p
@@ -43,6 +47,10 @@ class _Lib:
         f.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_float, _P, _P,
                       _P, _P, ctypes.c_int]
         f.restype = ctypes.c_int
+        f = getattr(L, prefix + "sample_mode_batch")
+        f.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_float, _P, _P,
+                      _P, _P, ctypes.c_int, ctypes.c_int]
+        f.restype = ctypes.c_int
         f = getattr(L, prefix + "sample_probs_batch")
         f.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_float, _P, _P, _P, ctypes.c_int]
         f.restype = ctypes.c_int
@@ -50,16 +58,24 @@ class _Lib:
         f.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_ulonglong, _P]
         f.restype = ctypes.c_int
 
-    def sample_batch(self, logits, temperature, topp, states, topp_rows=None, probs_out=False, nthreads=0):
+    def sample_batch(self, logits, temperature, topp, states, topp_rows=None, probs_out=False, nthreads=0,
+                     mode=0):
+        """sample() per row; mode 6 = sample_debug, mode 2 = do_sample (the
+        per-row calls of the reference's CUDA translation units)."""
         logits = np.ascontiguousarray(logits, dtype=np.float32)
         B, V = logits.shape
         ids = np.empty(B, dtype=np.int32)
         st = np.array(states, dtype=np.uint64, copy=True)
         tr = None if topp_rows is None else np.ascontiguousarray(topp_rows, dtype=np.float32)
         pr = np.empty_like(logits) if probs_out else None
-        getattr(self.L, self.prefix + "sample_batch")(
-            _fp(logits), B, V, V, temperature, topp, None if tr is None else _fp(tr), _fp(st), _fp(ids),
-            None if pr is None else _fp(pr), nthreads)
+        args = (_fp(logits), B, V, V, temperature, topp, None if tr is None else _fp(tr), _fp(st), _fp(ids),
+                None if pr is None else _fp(pr), nthreads)
+        if mode:
+            rc = getattr(self.L, self.prefix + "sample_mode_batch")(*args, mode)
+            if rc != 0:
+                raise ValueError(f"mode {mode} not available in {self.prefix}sample_mode_batch")
+        else:
+            getattr(self.L, self.prefix + "sample_batch")(*args)
         return (ids, st, pr) if probs_out else (ids, st)
 
     def sample_probs_batch(self, probs, topp, states, topp_rows=None, nthreads=0):

@@ -8,7 +8,11 @@
  * llama2_cublas_fp16.c:561-670 (identical to llama2.c:968-1105); nothing of
  * the reference is copied.  The result is oracle/_ref/libref_sampler.so,
  * used to pin the restatement in sampler_oracle.c and as the timed CPU
- * baseline ("kind": "reference").
+ * baseline ("kind": "reference").  Two more variants of the per-row call
+ * come from the reference's CUDA translation units (cut out by line range at
+ * build time, see oracle/Makefile): sample_debug (llama2_cublas.cu:5067-5111,
+ * linked here as cu_sample_debug) and do_sample (llama2_cublas_fp16.cu:
+ * 1178-1189, static there, reached through the fp16cu_do_sample wrapper).
  */
 #include <stdlib.h>
 #include <string.h>
@@ -37,6 +41,10 @@ int sample(Sampler* sampler, float* logits);
 int sample_mult(float* probabilities, int n, float coin);
 int sample_topp(float* probabilities, int n, float topp, ProbIndex* probindex, float coin);
 float random_f32(unsigned long long* state);
+/* The reference's sample_debug (llama2_cublas.cu:5067) under its build-time name. */
+int cu_sample_debug(Sampler* sampler, float* logits);
+/* The reference's do_sample (llama2_cublas_fp16.cu:1178) through the build-time wrapper. */
+int fp16cu_do_sample(Sampler* s, float* logits);
 
 static int clamp_threads(int nthreads) {
 #ifdef _OPENMP
@@ -66,6 +74,33 @@ int ref_sample_batch(const float* logits, int B, int V, long long ld, float temp
             build_sampler(&s, V, temperature, topp_rows ? topp_rows[r] : topp, states[r]);
             memcpy(row, logits + (size_t)r * (size_t)ld, (size_t)V * sizeof(float));
             ids[r] = sample(&s, row);
+            states[r] = s.rng_state;
+            if (probs_out) memcpy(probs_out + (size_t)r * V, row, (size_t)V * sizeof(float));
+            free_sampler(&s);
+        }
+        free(row);
+    }
+    return 0;
+}
+
+/* The per-row call of another reference translation unit over B rows, as
+ * ref_sample_batch does for sample(): mode 6 = sample_debug (NaN guard and
+ * greedy below 1e-6), mode 2 = do_sample (greedy below 1e-6).  Returns -1 for
+ * any other mode. */
+int ref_sample_mode_batch(const float* logits, int B, int V, long long ld, float temperature, float topp,
+                          const float* topp_rows, unsigned long long* states, int* ids, float* probs_out,
+                          int nthreads, int mode) {
+    if (mode != 6 && mode != 2) return -1;
+    nthreads = clamp_threads(nthreads);
+#pragma omp parallel num_threads(nthreads)
+    {
+        float* row = (float*)malloc((size_t)V * sizeof(float));
+#pragma omp for schedule(dynamic, 4)
+        for (int r = 0; r < B; ++r) {
+            Sampler s;
+            build_sampler(&s, V, temperature, topp_rows ? topp_rows[r] : topp, states[r]);
+            memcpy(row, logits + (size_t)r * (size_t)ld, (size_t)V * sizeof(float));
+            ids[r] = (mode == 6) ? cu_sample_debug(&s, row) : fp16cu_do_sample(&s, row);
             states[r] = s.rng_state;
             if (probs_out) memcpy(probs_out + (size_t)r * V, row, (size_t)V * sizeof(float));
             free_sampler(&s);

@@ -159,6 +159,28 @@ int oracle_sample(int n, float temperature, float topp, unsigned long long* stat
     return oracle_topp(logits, n, topp, scratch, coin);
 }
 
+/* Mode bits of the other per-row calls in the reference's CUDA translation
+ * units (the same values as the library's SAMPLER_FLAG_* bits). */
+#define ORACLE_GREEDY_BELOW_1E6 2 /* T < 1e-6f is greedy: do_sample, llama2_cublas_fp16.cu:1179;
+                                     sample_debug, llama2_cublas.cu:5089 */
+#define ORACLE_NAN_TOKEN1 4       /* any NaN logit -> token 1: sample_debug, llama2_cublas.cu:5071-5085 */
+
+/* sample() with the mode bits: mode 6 restates sample_debug
+ * (llama2_cublas.cu:5067-5111, whose diagnostic printf calls are left out),
+ * mode 2 restates do_sample (llama2_cublas_fp16.cu:1178-1189; its inlined
+ * cdf loop is sample_mult's).  The NaN test looks at the logits before any
+ * division; such a row returns 1 without drawing a coin or touching the
+ * buffer.  The greedy test `T < 1e-6f` takes T == 0 and every negative T. */
+int oracle_sample_mode(int n, float temperature, float topp, unsigned long long* state, float* logits,
+                       OracleProbIndex* scratch, int mode) {
+    if (mode & ORACLE_NAN_TOKEN1) {
+        for (int i = 0; i < n; ++i)
+            if (isnan(logits[i])) return 1;
+    }
+    if ((mode & ORACLE_GREEDY_BELOW_1E6) && temperature < 1e-6f) return oracle_argmax(logits, n);
+    return oracle_sample(n, temperature, topp, state, logits, scratch);
+}
+
 /* ---------------------------------------------------------------------------
  * Batch drivers (the reference has none: they loop its per-row call).
  * ------------------------------------------------------------------------- */
@@ -189,6 +211,28 @@ int oracle_sample_batch(const float* logits, int B, int V, long long ld, float t
             memcpy(row, logits + (size_t)r * (size_t)ld, (size_t)V * sizeof(float));
             const float tp = topp_rows ? topp_rows[r] : topp;
             ids[r] = oracle_sample(V, temperature, tp, &states[r], row, pi);
+            if (probs_out) memcpy(probs_out + (size_t)r * V, row, (size_t)V * sizeof(float));
+        }
+        free(row);
+        free(pi);
+    }
+    return 0;
+}
+
+/* oracle_sample_batch with the mode bits of oracle_sample_mode. */
+int oracle_sample_mode_batch(const float* logits, int B, int V, long long ld, float temperature, float topp,
+                             const float* topp_rows, unsigned long long* states, int* ids, float* probs_out,
+                             int nthreads, int mode) {
+    nthreads = clamp_threads(nthreads);
+#pragma omp parallel num_threads(nthreads)
+    {
+        float* row = (float*)malloc((size_t)V * sizeof(float));
+        OracleProbIndex* pi = (OracleProbIndex*)malloc((size_t)V * sizeof(OracleProbIndex));
+#pragma omp for schedule(dynamic, 4)
+        for (int r = 0; r < B; ++r) {
+            memcpy(row, logits + (size_t)r * (size_t)ld, (size_t)V * sizeof(float));
+            const float tp = topp_rows ? topp_rows[r] : topp;
+            ids[r] = oracle_sample_mode(V, temperature, tp, &states[r], row, pi, mode);
             if (probs_out) memcpy(probs_out + (size_t)r * V, row, (size_t)V * sizeof(float));
         }
         free(row);

@@ -11,6 +11,8 @@ Outputs (small JSON files, committed):
     topp.json        4096 sample_topp ids, per-row seeds 42+row, plus nucleus stats
     probs_in.json    sample_mult / sample_topp ids given the reference's own
                      probabilities (first 256 rows of mult and topp)
+    modes.json       sample_debug / do_sample ids and states on rows with NaNs,
+                     over temperatures around the 1e-6 greedy threshold
 """
 import hashlib
 import json
@@ -77,6 +79,20 @@ def main():
     json.dump(dict(mult_probs_sha=digest(pm), topp_probs_sha=digest(pt), mult_ids=ids_m.tolist(),
                    topp_ids=ids_t.tolist()),
               open(os.path.join(HERE, "probs_in.json"), "w"))
+    # sample_debug (llama2_cublas.cu:5067-5111) and do_sample
+    # (llama2_cublas_fp16.cu:1178-1189) of the reference's CUDA translation
+    # units, built from their sources into oracle/_ref (oracle/Makefile)
+    w = wl.debug_rows()
+    seeds = wl.row_seeds(w["logits"].shape[0])
+    cases = []
+    for mode, name in ((6, "sample_debug"), (2, "do_sample")):
+        for temp in w["temperatures"]:
+            for tp in w["topps"]:
+                ids, st, pr = ref.sample_batch(w["logits"], temp, tp, seeds, probs_out=True, mode=mode)
+                cases.append(dict(entry=name, mode=mode, temperature=temp, topp=tp, ids=ids.tolist(),
+                                  states_after=[int(x) for x in st], probs_sha=digest(pr)))
+    json.dump(dict(workload="debug_rows", input_sha=digest(w["logits"]), cases=cases),
+              open(os.path.join(HERE, "modes.json"), "w"))
     print("golden fixtures written to", HERE)
 
 

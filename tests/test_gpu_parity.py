@@ -31,7 +31,7 @@ def digest(a):
 
 
 def gpu_sample(pkg, x, temp, topp, seeds=None, topp_rows=None, temp_rows=None, coins=None, probs_in=False,
-               want_probs=False, ld=None):
+               want_probs=False, ld=None, mode=0):
     B, V = x.shape
     if ld is not None and ld != V:
         buf = torch.zeros(B, ld, device=DEV)
@@ -46,7 +46,7 @@ def gpu_sample(pkg, x, temp, topp, seeds=None, topp_rows=None, temp_rows=None, c
     probs = torch.empty(B, V, device=DEV) if want_probs else None
     flags = torch.full((B,), -1, dtype=torch.int32, device=DEV)
     ids = pkg.sample_batched(xt, temp, topp, st, topp_rows=tr, temperature_rows=te, coins=co, probs_out=probs,
-                             row_flags=flags, probs_in=probs_in)
+                             row_flags=flags, probs_in=probs_in, mode=mode)
     torch.cuda.synchronize()
     out = dict(ids=ids.cpu().numpy(), flags=flags.cpu().numpy())
     if st is not None:
@@ -421,3 +421,85 @@ def test_concurrent_samplers_on_threads(pkg):
     with ThreadPoolExecutor(4) as ex:
         got = list(ex.map(run, range(4)))
     assert got == want
+
+
+# ---------------------------------------------------------------------------
+# sample_debug (llama2_cublas.cu:5067-5111) and do_sample
+# (llama2_cublas_fp16.cu:1178-1189): the mode flags of the batched call and
+# the two single-row entry points, against tests/golden/modes.json (the
+# reference's own functions) and the oracle
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("want_probs", [True, False])
+def test_mode_rules_batched(pkg, orc, golden, want_probs):
+    w = pkg.workloads.debug_rows()
+    x = w["logits"]
+    B = x.shape[0]
+    seeds = pkg.workloads.row_seeds(B)
+    nan_rows = np.isnan(x).any(axis=1)
+    for case in golden["modes"]["cases"]:
+        mode, temp, topp = case["mode"], case["temperature"], case["topp"]
+        out = gpu_sample(pkg, x, temp, topp, seeds=seeds, want_probs=want_probs, mode=mode)
+        assert out["states"].tolist() == case["states_after"], case["entry"]
+        ref_ids, _, ref_p = orc.sample_batch(x, temp, topp, seeds, probs_out=True, mode=mode)
+        gids = np.array(case["ids"])
+        greedy = np.float32(temp) < np.float32(1e-6)
+        if mode & pkg.SAMPLER_FLAG_NAN_TOKEN1:
+            assert (out["ids"][nan_rows] == 1).all() and (out["flags"][nan_rows] & pkg.ROW_NAN).all()
+            if want_probs:  # the buffer keeps the logits
+                assert np.array_equal(out["probs"][nan_rows].view(np.uint32), x[nan_rows].view(np.uint32))
+            keep = ~nan_rows
+        else:
+            keep = np.ones(B, bool) if greedy else ~nan_rows  # NaN rows: undefined id in the reference
+        if greedy:
+            assert np.array_equal(out["ids"][keep], gids[keep])  # argmax: bit-exact
+        else:
+            check_e2e(orc, out["ids"][keep], gids[keep], ref_p[keep], seeds[keep], np.full(keep.sum(), topp))
+            if want_probs:
+                rel, _ = prob_rel_err(out["probs"][keep], ref_p[keep])
+                assert rel <= PROB_RTOL
+
+
+def test_mode_rules_greedy_threshold_per_row(pkg, golden):
+    """Per-row temperatures on both sides of 1e-6f in one batch: greedy rows
+    under GREEDY_BELOW_1E6 draw nothing; without the flag only T == 0 is."""
+    w = pkg.workloads.debug_rows()
+    x = w["logits"][~np.isnan(w["logits"]).any(axis=1)][:32]
+    temps = np.array([5e-7, 0.8, -0.5, 1e-6, 0.0, 9.9e-7, 0.7, 2e-6] * 4, np.float32)
+    seeds = np.arange(32, dtype=np.uint64) + 9
+    out = gpu_sample(pkg, x, 0.8, 0.9, seeds=seeds, temp_rows=temps, mode=pkg.MODE_DO_SAMPLE)
+    greedy = temps < np.float32(1e-6)
+    assert np.array_equal(out["states"][greedy], seeds[greedy])
+    assert (out["states"][~greedy] != seeds[~greedy]).all()
+    assert out["ids"][greedy].tolist() == [int(np.argmax(r)) for r in x[greedy]]
+    plain = gpu_sample(pkg, x, 0.8, 0.9, seeds=seeds, temp_rows=temps)
+    assert np.array_equal(plain["states"] == seeds, temps == 0.0)
+
+
+@pytest.mark.parametrize("entry,mode", [("sample_debug", 6), ("do_sample", 2)])
+def test_mode_rules_single_row_entry_points(pkg, orc, entry, mode):
+    """llama2_cublas.cu:5905 / llama2_cublas_fp16.cu:1268 call sites: one
+    Sampler advancing over rows, the buffer written back as the reference
+    leaves it."""
+    w = pkg.workloads.debug_rows(rows=22)
+    x = w["logits"]
+    for temp in (0.8, 5e-7, -0.5):
+        s = pkg.build_sampler(x.shape[1], temp, 0.9, 42)
+        st = np.array([42], np.uint64)
+        for r in range(x.shape[0]):
+            row = x[r].copy()
+            got = pkg.sample(s, row, entry=entry)
+            ref_ids, ref_st, ref_p = orc.sample_batch(x[r:r + 1], temp, 0.9, st, probs_out=True, mode=mode)
+            assert s.rng_state == int(ref_st[0]), (entry, temp, r)
+            nan_row = bool(np.isnan(x[r]).any())
+            if nan_row and mode & 4:
+                assert got == 1 and np.array_equal(row.view(np.uint32), x[r].view(np.uint32))
+            elif np.float32(temp) < np.float32(1e-6):
+                assert got == int(ref_ids[0]) and np.array_equal(row.view(np.uint32), x[r].view(np.uint32))
+            elif not nan_row:
+                rel, _ = prob_rel_err(row[None, :], ref_p)
+                assert rel <= PROB_RTOL
+                if got != int(ref_ids[0]):
+                    coin, _ = orc.coin(int(st[0]))
+                    assert orc.boundary_distance(ref_p[0], 0.9, coin) <= BOUNDARY
+            st = ref_st
+        pkg.free_sampler(s)

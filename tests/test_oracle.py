@@ -94,3 +94,26 @@ def test_oracle_matches_reference_random(ref, orc):
 
 def test_reference_baseline_threads(ref):
     assert ref.num_threads() >= 1
+
+
+def test_oracle_sample_debug_and_do_sample(pkg, orc, golden):
+    """The restated sample_debug / do_sample rules against the reference's own
+    functions (tests/golden/modes.json, written by the reference's code cut out
+    of llama2_cublas.cu and llama2_cublas_fp16.cu).  Rows whose top-p walk
+    finds no candidate (a NaN row without the NaN guard) read probindex[-1] in
+    the reference, an undefined id; there the oracle returns -1 and only the
+    state and the buffer are compared."""
+    w = pkg.workloads.debug_rows()
+    g = golden["modes"]
+    assert digest(w["logits"]) == g["input_sha"]
+    seeds = pkg.workloads.row_seeds(w["logits"].shape[0])
+    for case in g["cases"]:
+        ids, st, pr = orc.sample_batch(w["logits"], case["temperature"], case["topp"], seeds, probs_out=True,
+                                       mode=case["mode"])
+        defined = ids >= 0
+        assert np.array_equal(ids[defined], np.array(case["ids"])[defined]), case["entry"]
+        assert [int(x) for x in st] == case["states_after"]
+        assert digest(pr) == case["probs_sha"]
+        if case["mode"] & 4:  # NaN rows: token 1, no draw
+            nan_rows = np.isnan(w["logits"]).any(axis=1)
+            assert (ids[nan_rows] == 1).all() and np.array_equal(st[nan_rows], seeds[nan_rows])
