@@ -142,8 +142,14 @@ size_t sampler_workspace_bytes(int batch, int vocab_size);
  *   out_ids          [batch] int32 token ids
  *   probs_out        [batch, vocab_size] or NULL: the probabilities sample()
  *                    leaves in its buffer (softmax output; logits when greedy)
- *   row_flags        [batch] or NULL: SAMPLER_ROW_* bits per row
- *   workspace        NULL (library-managed) or >= sampler_workspace_bytes()
+ *   row_flags        [batch] or NULL: SAMPLER_ROW_* bits per row; the only
+ *                    report of a device timeout (SAMPLER_ROW_TIMEOUT, id 0 on
+ *                    every unfinished row), since the call does not synchronize
+ *   workspace        NULL (library-managed: one workspace per stream, created
+ *                    on the stream's first call and kept until the process
+ *                    exits, so calls on different streams may overlap) or a
+ *                    caller buffer >= sampler_workspace_bytes(), which calls
+ *                    that may overlap on the GPU must not share
  * Per row it follows sample() (llama2.c:1082-1105) exactly: greedy when
  * temperature == 0, else /T, softmax, coin, then sample_mult when topp <= 0
  * or topp >= 1, else sample_topp (with SAMPLER_MODE_SAMPLE_DEBUG or
@@ -191,8 +197,8 @@ const char* sampler_last_error(void);
  *   logits_out fp32 [batch, vocab_size] or NULL (then library-managed)
  * Other arguments as in sampler_batched().  Asynchronous on `stream`.
  * The per-chunk statistics (and the logits when logits_out is NULL) live in
- * buffers the library keeps per device, so fused calls that may overlap on
- * one GPU (different streams or threads) must be serialized. */
+ * buffers the library keeps per stream (created on the stream's first call),
+ * so fused calls on different streams may overlap. */
 int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, const void* wcls, int batch,
                             int dim, const float* temperature_rows, const float* topp_rows, const float* coins,
                             unsigned long long* rng_state, int* out_ids, float* logits_out, int* row_flags,
@@ -230,6 +236,14 @@ int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* 
 int sampler_gather_rows(const float* table, int table_rows, int dim, const int* ids, int batch, float* out,
                         void* stream);
 
+/* Failure-detection self-test (no counterpart in the reference): runs the
+ * row kernel on one row with its first bounded device wait made to run out
+ * after `polls` polls (a barrier that no copy targets, so nothing is left in
+ * flight), synchronizes, and reports it as a real timeout is reported:
+ * returns SAMPLER_E_DEVICE and sets *row_flag to SAMPLER_ROW_TIMEOUT.  The
+ * device stays usable; later calls run normally.  polls in [1, 2^24]. */
+int sampler_selftest_wait_timeout(unsigned polls, int* row_flag);
+
 /* Largest vocabulary sampler_batched_noalloc accepts. */
 #define SAMPLER_NOALLOC_MAX_VOCAB 32768
 
@@ -248,7 +262,11 @@ int sampler_gather_rows(const float* table, int table_rows, int dim, const int* 
  *  - Every call shares the array (it keeps the last call's contents), so
  *    calls that overlap on the GPU -- different streams, or threads using the
  *    same device -- race; serialize them.
- *  - Returns status codes only; sampler_last_error() is not updated. */
+ *  - Returns status codes only; sampler_last_error() is not updated.
+ *  - The call does not synchronize, so a device timeout (a bounded wait that
+ *    ran out) is reported only through row_flags: every row the kernel did
+ *    not finish gets SAMPLER_ROW_TIMEOUT and id 0.  Callers that need to see
+ *    it pass row_flags. */
 int sampler_batched_noalloc(const SamplerBatchConfig* cfg, const float* logits, int batch, long long ld,
                             const float* temperature_rows, const float* topp_rows, const float* coins,
                             unsigned long long* rng_state, int* out_ids, float* probs_out, int* row_flags,

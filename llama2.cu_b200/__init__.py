@@ -28,6 +28,7 @@ EXPORTED_SYMBOLS = [
     "sampler_nccl_get_unique_id", "sampler_nccl_comm_init", "sampler_nccl_allgather_ids",
     "sampler_nccl_comm_destroy", "sampler_batched_noalloc", "classifier_sample_fused",
     "classifier_logits", "rmsnorm_bf16", "classifier_rmsnorm_sample_fused", "sampler_gather_rows",
+    "sampler_selftest_wait_timeout",
 ]
 
 
@@ -123,6 +124,8 @@ def lib():
     L.classifier_rmsnorm_sample_fused.restype = c_int
     L.sampler_gather_rows.argtypes = [P, c_int, c_int, P, c_int, P, P]
     L.sampler_gather_rows.restype = c_int
+    L.sampler_selftest_wait_timeout.argtypes = [ctypes.c_uint, ctypes.POINTER(c_int)]
+    L.sampler_selftest_wait_timeout.restype = c_int
     _lib = L
     return L
 

@@ -56,9 +56,10 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
     return ok != 0;
 }
 
-// Bounded wait: gives up after kSpinLimit polls instead of hanging the SM.
-__device__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity) {
-    for (unsigned i = 0; i < kSpinLimit; ++i) {
+// Bounded wait: gives up after `limit` polls (kSpinLimit by default)
+// instead of hanging the SM.
+__device__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity, unsigned limit = kSpinLimit) {
+    for (unsigned i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if (i > 32) __nanosleep(64);
     }

@@ -90,6 +90,11 @@ extern "C" int sampler_batched_noalloc(const SamplerBatchConfig* cfg, const floa
     if (ctas > d->num_sms) ctas = d->num_sms;
     if (ctas > batch) ctas = batch;
 
+    // The error word starts each call at zero (a stream-ordered memset of the
+    // array's header; no allocation).  Its value is not read back: the call
+    // does not synchronize, so a timeout shows only in row_flags.
+    if (cudaMemsetAsync(d->base, 0, sizeof(int), (cudaStream_t)stream) != cudaSuccess) return SAMPLER_E_CUDA;
+
     b2s::RowLaunch p{};
     p.logits = logits;
     p.ld = ld;

@@ -39,6 +39,7 @@ struct StreamSmem {
     int flag;
     int dbin;
     int sort_next;  // next group of 32 bins to sort
+    int next_row;   // the row this CTA takes next
     int n_pairs;    // equal-p neighbours found by the p pass
     int pairs[kPairCap];
     int ksel;
@@ -636,6 +637,18 @@ __device__ void sort_bins(StreamSmem& sm, unsigned long long* kb, int D, int K, 
     }
 }
 
+// The next row of this CTA.  With a counter, rows past the first gridDim.x
+// are handed out in order of demand: rows differ in cost (nucleus size, the
+// serial sums' binade crossings), and a fixed stride leaves the CTAs that drew
+// heavy rows finishing last.  Without one, the fixed stride.
+__device__ __forceinline__ int next_row(const RowLaunch& p, StreamSmem& sm, int row) {
+    if (!p.row_counter) return row + gridDim.x;
+    __syncthreads();  // every thread has read sm.next_row of the previous row
+    if (threadIdx.x == 0) sm.next_row = (int)gridDim.x + atomicAdd(p.row_counter, 1);
+    __syncthreads();
+    return sm.next_row;
+}
+
 __device__ void defer_row_s(const RowLaunch& p, int row) {
     const int k = atomicAdd(p.defer_count, 1);
     p.defer_rows[k] = row;
@@ -717,7 +730,7 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
     // per-CTA L2-resident scratch for nuclei above the on-chip capacity
     unsigned long long* super = p.workspace + (long long)blockIdx.x * p.ws_stride;
 
-    for (int row = blockIdx.x; row < p.batch; row += gridDim.x) {
+    for (int row = blockIdx.x; row < p.batch; row = next_row(p, sm, row)) {
         Ctx c;
         c.src = p.logits + (long long)row * p.ld;
         c.V = V;

@@ -159,7 +159,7 @@ int ensure_row(DeviceCtx* c, int V) {
 
 int row_ctas(const DeviceCtx* c, int batch) { return batch < c->num_sms ? batch : c->num_sms; }
 
-// Workspace layout: [deferred-row count (16 B)][deferred rows: batch int32,
+// Workspace layout: [deferred-row count, row counter (16 B)][deferred rows: batch int32,
 // padded to 16 B][general kernel: ctas x pow2(V) u64 sort scratch]
 // [streaming kernel: stream_ctas x V u64 candidate lists].
 size_t defer_bytes(int batch) { return 16 + (((size_t)batch * sizeof(int) + 15) & ~(size_t)15); }
@@ -276,8 +276,9 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
                           ((uintptr_t)probs_out & 15u) == 0;
     int launches = 0;
     if (streamed) {
-        B2S_CUDA(cudaMemsetAsync(defer_count, 0, sizeof(int), stream));
+        B2S_CUDA(cudaMemsetAsync(defer_count, 0, 2 * sizeof(int), stream));  // count and row counter
         b2s::RowLaunch q = p;
+        q.row_counter = defer_count + 1;
         q.workspace = stream_ws;
         q.ws_stride = (long long)stream_stride(V);
         q.stats = stats;
@@ -720,6 +721,42 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
     B2S_CUDA(cudaStreamSynchronize(c->streams[0]));
     B2S_CUDA(cudaStreamSynchronize(c->streams[1]));
     g_last_launches = launches;
+    return check_device_word(c);
+}
+
+// Failure-detection self-test: the row kernel on one zero row whose staging
+// issues no copy, so its first bounded wait runs out after `polls` polls; the
+// timeout is reported the way a real one is.
+int sampler_selftest_wait_timeout(unsigned polls, int* row_flag) {
+    g_last_launches = 0;
+    if (polls == 0 || polls > (1u << 24) || !row_flag)
+        return fail(SAMPLER_E_INVALID, "polls must be in [1, 2^24] and row_flag non-NULL");
+    DeviceCtx* c = nullptr;
+    int rc = get_ctx(&c);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> host_lock(c->host_mu);
+    constexpr int V = 64;
+    if (ensure_row(c, V)) return SAMPLER_E_CUDA;
+    cudaStream_t s = c->stream;
+    int* d_flag = c->d_id + 1;  // d_id holds 4 ints: [0] the id, [1] the row flag
+    B2S_CUDA(cudaMemsetAsync(c->d_row, 0, V * sizeof(float), s));
+    B2S_CUDA(cudaMemsetAsync(c->d_id, 0xFF, 2 * sizeof(int), s));
+    b2s::RowLaunch p{};
+    p.logits = c->d_row;
+    p.ld = V;
+    p.batch = 1;
+    p.vocab = V;
+    p.temperature = 0.0f;
+    p.topp = 0.9f;
+    p.out_ids = c->d_id;
+    p.row_flags = d_flag;
+    p.error_word = c->error_word;
+    p.wait_test = polls;
+    const int n = b2s::launch_row_sampler(p, 1, s);
+    if (n < 0) return fail(SAMPLER_E_CUDA, "row sampler launch: %s", cudaGetErrorString((cudaError_t)(-n)));
+    g_last_launches = n;
+    B2S_CUDA(cudaMemcpyAsync(row_flag, d_flag, sizeof(int), cudaMemcpyDeviceToHost, s));
+    B2S_CUDA(cudaStreamSynchronize(s));
     return check_device_word(c);
 }
 

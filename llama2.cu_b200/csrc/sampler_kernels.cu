@@ -823,7 +823,9 @@ __global__ void __launch_bounds__(kRowThreads, 1) row_sampler_kernel(RowLaunch p
 
         // 1. stage the row
         if (vbody > 0) {
-            if (tid == 0) {
+            // the self-test issues no copy for its first row: nothing arrives
+            const bool stall = p.wait_test != 0 && it == (int)blockIdx.x;
+            if (tid == 0 && !stall) {
                 fence_proxy_async_smem();
                 mbar_arrive_expect_tx(&sm.mbar[0], (unsigned)vbody * 4u);
                 const int part = ((vbody / kTmaParts) + 3) & ~3;
@@ -832,16 +834,18 @@ __global__ void __launch_bounds__(kRowThreads, 1) row_sampler_kernel(RowLaunch p
                     bulk_copy_g2s(sm.row + off, src + off, (unsigned)len * 4u, &sm.mbar[0]);
                 }
             }
-            const bool ok = mbar_wait_bounded(&sm.mbar[0], phase);
+            const bool ok = mbar_wait_bounded(&sm.mbar[0], phase, p.wait_test ? p.wait_test : kSpinLimit);
             phase ^= 1u;
             if (!__syncthreads_and(ok)) {
-                // The copy did not land in time: report, drain (bounded), stop.
-                if (tid == 0) {
-                    atomicExch(p.error_word, 1);
-                    if (p.row_flags) p.row_flags[row] = kFlagTimeout;
-                    p.out_ids[row] = 0;
+                // The copy did not land in time: report, wait (bounded) for the
+                // copies in flight, mark this CTA's unfinished rows, stop.
+                if (tid == 0) atomicExch(p.error_word, 1);
+                if (!stall) mbar_wait_bounded(&sm.mbar[0], phase ^ 1u);
+                for (int j = it + tid * (int)gridDim.x; j < nrows; j += (int)(blockDim.x * gridDim.x)) {
+                    const int r = p.row_list ? p.row_list[j] : j;
+                    if (p.row_flags) p.row_flags[r] = kFlagTimeout;
+                    p.out_ids[r] = 0;
                 }
-                mbar_wait_bounded(&sm.mbar[0], phase ^ 1u);
                 return;
             }
         }

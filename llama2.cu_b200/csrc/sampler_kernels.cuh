@@ -32,6 +32,12 @@ struct RowLaunch {
     int greedy_eps;               // rows with temperature < 1e-6f are greedy (do_sample, sample_debug)
     int nan_token1;               // rows holding a NaN logit give token 1, no draw (sample_debug)
     int* error_word;              // device word, set on bounded-wait timeout
+    // Failure-detection self-test only (0 otherwise): the first row's staging
+    // issues no copy, so its bounded wait runs out after this many polls.
+    unsigned wait_test;
+    // streaming kernel: next row to take (rows handed out in order of demand
+    // past the first gridDim.x); nullptr keeps the fixed stride
+    int* row_counter;
     // deferred rows: the streaming kernel appends rows it leaves to the
     // general kernel; the general kernel then walks row_list[0..*row_count)
     int* defer_count;

@@ -188,3 +188,56 @@ def test_device_resident_decode_loop_in_a_cuda_graph(pkg):
     got_ids, got_st = run(lambda *_: graph.replay(), x, st, ids)
     assert torch.equal(got_ids, want_ids) and torch.equal(got_st, want_st)
     assert len(set(want_ids[-1].tolist())) > 1  # the loop really samples
+
+
+def test_fused_full_decode_batch_seeded_operands(pkg, orc):
+    """The fused workload as configured: 8192 hidden states of dim 4096
+    (seed-4 numpy operands, bf16) against wcls [32000, 4096], T = 0.8,
+    topp 0.9.  Logits against an fp32 matmul of the same bf16 operands in row
+    blocks; ids, states and flags equal sampler_batched on the fused call's own
+    logits for every row; 1024 rows spread over the batch pass the end-to-end
+    rule against the oracle."""
+    f = pkg.workloads.fused()
+    h = torch.from_numpy(f["hidden"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    w = torch.from_numpy(f["wcls"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    B, V = h.shape[0], w.shape[0]
+    assert (B, h.shape[1], V) == (8192, 4096, 32000)
+    seeds = pkg.workloads.row_seeds(B, seed=f["seed"])
+    out = fused(pkg, h, w, f["temperature"], f["topp"], seeds)
+    for b0 in range(0, B, 1024):
+        check_logits(h[b0:b0 + 1024], w, out["logits"][b0:b0 + 1024])
+    ref = unfused(pkg, out["logits"], f["temperature"], f["topp"], seeds)
+    assert np.array_equal(out["ids"], ref["ids"])
+    assert np.array_equal(out["states"], ref["states"])
+    assert np.array_equal(out["flags"], ref["flags"])
+    rows = np.arange(0, B, 8)
+    x = out["logits"][torch.from_numpy(rows).to(DEV)].cpu().numpy()
+    ref_ids, ref_st, ref_p = orc.sample_batch(x, f["temperature"], f["topp"], seeds[rows], probs_out=True)
+    assert np.array_equal(out["states"][rows], ref_st)
+    check_e2e(orc, out["ids"][rows], ref_ids, ref_p, seeds[rows], np.full(len(rows), f["topp"]))
+
+
+def test_device_logits_through_dump_files(pkg, orc, tmp_path):
+    """The classifier's device logits written as the reference's -DDUMP_LOGITS
+    files (a raw fp32 row per step, the JSON id list) and read back the way its
+    analysis script reads them: the same bits, and the ids the fused call
+    sampled from them."""
+    B, D, V = 6, 4096, 32000
+    h, w = operands(B, D, V, seed=77)
+    logits = pkg.classifier_logits(h, w)
+    seeds = pkg.workloads.row_seeds(B)
+    st = torch.from_numpy(seeds.view(np.int64).copy()).to(DEV)
+    ids = pkg.classifier_sample_fused(h, w, 0.8, 0.9, st)
+    torch.cuda.synchronize()
+    d = pkg.dumps
+    lp, ip = tmp_path / "ours.bin", tmp_path / "ids.json"
+    for step in range(B):  # one decode step per row, as the generate loop dumps them
+        d.append_logits(lp, logits[step], first=(step == 0))
+        d.append_token_ids(ip, ids[step:step + 1], first=(step == 0))
+    back = np.fromfile(lp, dtype=np.float32).reshape(-1, V)
+    assert np.array_equal(back.view(np.uint32), logits.cpu().numpy().view(np.uint32))
+    assert np.array_equal(d.load_logits(lp, V), back)
+    import json
+    assert json.load(open(ip)) == ids.cpu().numpy().tolist()
+    ref_ids, _, ref_p = orc.sample_batch(back, 0.8, 0.9, seeds, probs_out=True)
+    check_e2e(orc, ids.cpu().numpy(), ref_ids, ref_p, seeds, np.full(B, 0.9))
