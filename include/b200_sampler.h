@@ -232,7 +232,10 @@ int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* 
  * gives a zero row.  Device buffers; asynchronous on `stream`.  With the
  * library's buffers allocated by a first call, a whole decode step
  * (sampler_seed_states / classifier_sample_fused / sampler_gather_rows) can
- * be captured in a CUDA graph. */
+ * be captured in a CUDA graph: a call captured on a stream that has no
+ * library buffers of its own yet (nothing is allocated during a capture)
+ * uses those of the last call made outside a capture, so replays of that
+ * graph must not overlap calls on that call's stream. */
 int sampler_gather_rows(const float* table, int table_rows, int dim, const int* ids, int batch, float* out,
                         void* stream);
 

@@ -94,6 +94,7 @@ struct DeviceCtx {
     int rows_cap = 0;
     // per-stream buffers, created on a stream's first call and kept until exit
     std::vector<StreamBufs*> per_stream;
+    StreamBufs* last_eager = nullptr;  // the set the last call outside a stream capture used
 };
 
 std::mutex g_mu;
@@ -143,6 +144,31 @@ StreamBufs* stream_bufs(DeviceCtx* c, cudaStream_t stream) {
     b->stream = stream;
     c->per_stream.push_back(b);
     return b;
+}
+
+bool stream_capturing(cudaStream_t s) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    return cudaStreamIsCapturing(s, &st) == cudaSuccess && st != cudaStreamCaptureStatusNone;
+}
+
+// The set a call on `stream` uses (callers hold g_mu and then grow the member
+// they need with ensure_buf, which allocates).  Nothing can be allocated while
+// a stream is being captured into a CUDA graph, so a capturing stream whose
+// own set is too small (torch captures on a side stream of its own) borrows
+// the set of the last call made outside a capture, when that one is large
+// enough: the graph's replays then use those buffers.  `fits` tells whether a
+// set already holds what the call needs.  Returns nullptr when a capture finds
+// no large enough set (make one eager call of the same size first).
+template <class Fits>
+StreamBufs* bufs_for_call(DeviceCtx* c, cudaStream_t stream, const Fits& fits) {
+    StreamBufs* b = stream_bufs(c, stream);
+    if (!stream_capturing(stream)) {
+        c->last_eager = b;
+        return b;
+    }
+    if (fits(b)) return b;
+    if (c->last_eager && fits(c->last_eager)) return c->last_eager;
+    return nullptr;
 }
 
 int ensure_row(DeviceCtx* c, int V) {
@@ -234,7 +260,8 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
         ws = static_cast<unsigned long long*>(workspace);
     } else {
         std::lock_guard<std::mutex> lk(g_mu);
-        StreamBufs* b = stream_bufs(c, stream);
+        StreamBufs* b = bufs_for_call(c, stream, [&](StreamBufs* x) { return x->workspace_bytes >= need; });
+        if (!b) return fail(SAMPLER_E_WORKSPACE, "no library workspace of %zu bytes during a stream capture", need);
         rc = ensure_buf(&b->workspace, &b->workspace_bytes, need);
         if (rc) return rc;
         ws = b->workspace;
@@ -524,7 +551,10 @@ int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, c
     float4* stats = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
-        StreamBufs* b = stream_bufs(c, (cudaStream_t)stream);
+        StreamBufs* b = bufs_for_call(c, (cudaStream_t)stream, [&](StreamBufs* x) {
+            return x->stats_cap >= nst * sizeof(float4) && (logits || x->flogits_cap >= nlog * sizeof(float));
+        });
+        if (!b) return fail(SAMPLER_E_WORKSPACE, "no library buffers for %d rows during a stream capture", batch);
         if (!logits) {
             rc = ensure_buf(&b->flogits, &b->flogits_cap, nlog * sizeof(float));
             if (rc) return rc;
@@ -584,7 +614,8 @@ int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* 
     void* h = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
-        StreamBufs* b = stream_bufs(c, (cudaStream_t)stream);
+        StreamBufs* b = bufs_for_call(c, (cudaStream_t)stream, [&](StreamBufs* x) { return x->hnorm_cap >= need; });
+        if (!b) return fail(SAMPLER_E_WORKSPACE, "no library buffers for %d rows during a stream capture", batch);
         rc = ensure_buf(&b->hnorm, &b->hnorm_cap, need);
         if (rc) return rc;
         h = b->hnorm;
