@@ -601,14 +601,15 @@ __device__ __forceinline__ float fma_bf16_hi(uint32_t a2, uint32_t b2, float c) 
 }
 
 // acc[r][b] += W[row r, 8 elements] . H[b, same 8 elements] for one K step,
-// element by element in K order.
-template <int NB>
+// element by element in K order.  H in global memory, or in shared memory
+// when the kernel formed it (the folded RMSNorm).
+template <int NB, bool kSharedH>
 __device__ __forceinline__ void gemv_step(float (&acc)[kVRows][NB], const uint4 (&w)[kVRows], const uint4* h,
                                           long long rs, int batch) {
     uint32_t hq[NB][4];
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-        const uint4 q = (b < batch) ? __ldg(h + b * rs) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 q = (b < batch) ? (kSharedH ? h[b * rs] : __ldg(h + b * rs)) : make_uint4(0u, 0u, 0u, 0u);
         hq[b][0] = q.x;
         hq[b][1] = q.y;
         hq[b][2] = q.z;
@@ -627,15 +628,60 @@ __device__ __forceinline__ void gemv_step(float (&acc)[kVRows][NB], const uint4 
     }
 }
 
+constexpr int kNormThreads = 256;  // the RMSNorm kernel's CTA (its summation order)
+constexpr int kFoldMaxDim = 16384;  // RMSNorm folded into the GEMV up to this dim
+
+// The bf16 operand rows bf16(w * (r * x)), r = 1/sqrt(mean(x^2) + 1e-5), of
+// `nb` fp32 rows into shared memory, by a CTA of kVWarps warps, with the
+// arithmetic of rmsnorm_bf16_kernel in the same order: each thread plays the
+// kNormThreads/(kVWarps*32) threads of that kernel with its index modulo
+// kVWarps*32 (fma over j = t, t + 256, ..), then the same warp and block sums.
 template <int NB>
+__device__ void fold_rmsnorm_rows(const float* x, const float* w, int dim, int nb, __nv_bfloat16* hs) {
+    constexpr int kPlay = kNormThreads / (kVWarps * 32);  // threads of the norm kernel each thread plays
+    __shared__ float red[NB][kNormThreads / 32];
+    __shared__ float rr[NB];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int b = 0; b < nb; ++b) {
+        const float* xr = x + (long long)b * dim;
+        float ss[kPlay];
+#pragma unroll
+        for (int k = 0; k < kPlay; ++k) {
+            ss[k] = 0.0f;
+            for (int j = tid + k * kVWarps * 32; j < dim; j += kNormThreads) ss[k] = __fmaf_rn(xr[j], xr[j], ss[k]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) ss[k] += __shfl_xor_sync(kFullMask, ss[k], o);
+            if (lane == 0) red[b][warp + k * kVWarps] = ss[k];
+        }
+    }
+    __syncthreads();
+    if (tid < nb) {
+        float tot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kNormThreads / 32; ++i) tot += red[tid][i];
+        rr[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)dim), 1e-5f)));
+    }
+    __syncthreads();
+    for (int b = 0; b < nb; ++b) {
+        const float* xr = x + (long long)b * dim;
+        const float r = rr[b];
+        for (int j = tid; j < dim; j += kVWarps * 32)
+            hs[(long long)b * dim + j] = __float2bfloat16_rn(__fmul_rn(w[j], __fmul_rn(r, xr[j])));
+    }
+    __syncthreads();
+}
+
+template <int NB, bool kFold>
 __global__ void __launch_bounds__(kVWarps * 32, 8) classifier_gemv_kernel(GemmLaunch p) {
     __shared__ float part[kVWarps][NB][32];
+    extern __shared__ __align__(16) unsigned char gemv_dyn[];  // the folded operand rows (kFold)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int v0 = blockIdx.x * 32;
     const long long rs = p.dim >> 3;  // uint4 per row (dim % 8 == 0)
     const int steps = (p.dim + 255) >> 8;
     const uint4* W = reinterpret_cast<const uint4*>(p.w);
-    const uint4* H = reinterpret_cast<const uint4*>(p.h) + lane;
+    if (kFold) fold_rmsnorm_rows<NB>(p.x_f32, p.norm_w, p.dim, p.batch, reinterpret_cast<__nv_bfloat16*>(gemv_dyn));
+    const uint4* H = reinterpret_cast<const uint4*>(kFold ? static_cast<const void*>(gemv_dyn) : p.h) + lane;
     const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1;
     float mine[NB];
 #pragma unroll
@@ -659,8 +705,8 @@ __global__ void __launch_bounds__(kVWarps * 32, 8) classifier_gemv_kernel(GemmLa
                 w1[r] = ok1 ? __ldcs(wr + r * rs + s * 32) : make_uint4(0u, 0u, 0u, 0u);
                 w2[r] = ok2 ? __ldcs(wr + r * rs + s2 * 32) : make_uint4(0u, 0u, 0u, 0u);
             }
-            if (ok1) gemv_step<NB>(acc, w1, H + s * 32, rs, p.batch);
-            if (ok2) gemv_step<NB>(acc, w2, H + s2 * 32, rs, p.batch);
+            if (ok1) gemv_step<NB, kFold>(acc, w1, H + s * 32, rs, p.batch);
+            if (ok2) gemv_step<NB, kFold>(acc, w2, H + s2 * 32, rs, p.batch);
         }
         // rows r of this pass: lanes with bits (4, 3) = (r >> 1, r & 1) end
         // with the warp's full sum of row r
@@ -739,7 +785,6 @@ bool make_tmap(CUtensorMap* m, const void* base, int rows, int dim, int box_rows
 // operand.  One 256-thread CTA per row; the sum of squares is a tree sum
 // (the reference's is serial), so o can differ from the reference's in the
 // last bit of the fp32 value before the bf16 rounding.
-constexpr int kNormThreads = 256;
 
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_bf16_kernel(const float* x, const float* w, int dim,
                                                                     __nv_bfloat16* out) {
@@ -822,20 +867,46 @@ int launch_classifier_gemm_pair(const GemmLaunch& p, int num_sms, cudaStream_t s
     return e == cudaSuccess ? 1 : -(int)e;
 }
 
+bool gemm_folds_rmsnorm(int batch, int dim) { return batch >= 1 && batch <= kGemvMaxBatch && dim <= kFoldMaxDim; }
+
 int launch_classifier_gemv(const GemmLaunch& p, cudaStream_t stream) {
+    const bool fold = p.x_f32 != nullptr;
     if (p.batch < 1 || p.batch > kGemvMaxBatch || (p.dim & 7) || (p.vocab & 31) ||
-        ((reinterpret_cast<uintptr_t>(p.h) | reinterpret_cast<uintptr_t>(p.w)) & 15))
+        ((reinterpret_cast<uintptr_t>(fold ? nullptr : p.h) | reinterpret_cast<uintptr_t>(p.w)) & 15) ||
+        (fold && (!p.norm_w || p.dim > kFoldMaxDim)))
         return -(int)cudaErrorInvalidValue;
     const int grid = p.vocab / 32;
-    if (p.batch == 1)
-        classifier_gemv_kernel<1><<<grid, kVWarps * 32, 0, stream>>>(p);
-    else
-        classifier_gemv_kernel<2><<<grid, kVWarps * 32, 0, stream>>>(p);
+    const size_t dyn = fold ? (size_t)p.batch * p.dim * 2 : 0;
+    if (fold && dyn > 48 * 1024) {  // above the default: opt in once per device and shape
+        static std::atomic<unsigned long long> attr_done{0};
+        int dev = 0;
+        cudaError_t e0 = cudaGetDevice(&dev);
+        if (e0 != cudaSuccess) return -(int)e0;
+        const unsigned long long bit = 1ull << (dev & 63);
+        if (!(attr_done.load() & bit)) {
+            const int mx = 2 * kFoldMaxDim * 2;
+            cudaError_t e1 = cudaFuncSetAttribute(classifier_gemv_kernel<1, true>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+            cudaError_t e2 = cudaFuncSetAttribute(classifier_gemv_kernel<2, true>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+            if (e1 != cudaSuccess) return -(int)e1;
+            if (e2 != cudaSuccess) return -(int)e2;
+            attr_done.fetch_or(bit);
+        }
+    }
+    if (p.batch == 1) {
+        if (fold) classifier_gemv_kernel<1, true><<<grid, kVWarps * 32, dyn, stream>>>(p);
+        else classifier_gemv_kernel<1, false><<<grid, kVWarps * 32, 0, stream>>>(p);
+    } else {
+        if (fold) classifier_gemv_kernel<2, true><<<grid, kVWarps * 32, dyn, stream>>>(p);
+        else classifier_gemv_kernel<2, false><<<grid, kVWarps * 32, 0, stream>>>(p);
+    }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 1 : -(int)e;
 }
 
 int launch_classifier_gemm(const GemmLaunch& p, int num_sms, cudaStream_t stream) {
+    if (p.x_f32 && !gemm_folds_rmsnorm(p.batch, p.dim)) return -(int)cudaErrorInvalidValue;
     // One or two rows stream W on CUDA cores.
     if (p.batch <= kGemvMaxBatch) return launch_classifier_gemv(p, stream);
     // Batches of more than one 128-row block use CTA pairs (half the staged

@@ -18,8 +18,12 @@ constexpr int kBinsPerThread = kBins / kST;
 constexpr int kWalkDirect = 512;
 constexpr int kPairCap = 128;   // equal-p neighbour positions recorded for the tie fix  // nuclei walked element by element; larger ones by chunk functions
 
-// chunk entry: x=L0 y=L1 z=bits(pbits | flags | alt<<8 | side<<16) w=bits(eb)
-constexpr uint32_t kFClean = 4u, kFValid = 8u, kFAlt = 16u;
+// chunk entry: x=L0 y=L1 z=bits(pbits | flags | alt<<8 | side<<16 | run end<<24) w=bits(eb)
+// A run chunk (kFRun) is clean in its guessed binade with no alternative; its
+// entry holds the composition of the chunks from it to the end of its run
+// (the consecutive run chunks of one binade among the warp's 32), and bits
+// 24-28 the lane of that last chunk.  Other chunks hold their own function.
+constexpr uint32_t kFClean = 4u, kFValid = 8u, kFAlt = 16u, kFRun = 32u;
 
 struct StreamSmem {
     unsigned long long kbuf[kKCap];
@@ -39,7 +43,7 @@ struct StreamSmem {
     int flag;
     int dbin;
     int sort_next;  // next group of 32 bins to sort
-    int next_row;   // the row this CTA takes next
+    int next_row[2];  // the row this CTA takes next (two slots: claimed one row ahead)
     int n_pairs;    // equal-p neighbours found by the p pass
     int pairs[kPairCap];
     int ksel;
@@ -64,6 +68,7 @@ struct Ctx {
     float T, rT;
     float max_x;
     bool unit;
+    bool v32;  // rows 32-byte aligned: chunks load as 32-byte vectors
 };
 
 // ---------------------------------------------------------------------------
@@ -125,6 +130,32 @@ __device__ __forceinline__ xm::ChainFn fn_shfl_up(const xm::ChainFn& f, int o) {
     return xm::ChainFn{__shfl_up_sync(kFullMask, f.L0, o), __shfl_up_sync(kFullMask, f.L1, o),
                        __shfl_up_sync(kFullMask, f.pbits, o)};
 }
+__device__ __forceinline__ xm::ChainFn fn_shfl_down(const xm::ChainFn& f, int o) {
+    return xm::ChainFn{__shfl_down_sync(kFullMask, f.L0, o), __shfl_down_sync(kFullMask, f.L1, o),
+                       __shfl_down_sync(kFullMask, f.pbits, o)};
+}
+
+// Segmented suffix composition across the warp's lanes: lane i returns
+// f_i then f_(i+1) ... up to the last lane of its run (`end`), where `link`
+// says that lane i's run continues into lane i + 1.  Lanes outside a run pass
+// the identity with link = false.
+__device__ __forceinline__ xm::ChainFn warp_run_suffix(xm::ChainFn f, bool link, int& end) {
+    const int lane = threadIdx.x & 31;
+    end = lane;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const xm::ChainFn g = fn_shfl_down(f, o);
+        const int link_g = __shfl_down_sync(kFullMask, (int)link, o);
+        const int end_g = __shfl_down_sync(kFullMask, end, o);
+        if (link && lane + o < 32) {  // f covers [lane, lane + o) and the run goes on
+            f = xm::chain_compose(f, g);
+            link = link_g != 0;
+            end = end_g;
+        }
+    }
+    return f;
+}
+
 __device__ __forceinline__ xm::ChainFn warp_incl_compose(xm::ChainFn f) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
@@ -230,77 +261,98 @@ __device__ __forceinline__ float exact_e(const Ctx& c, const StreamSmem& sm, flo
 // Replays chunk t exactly starting from s (warp 0): kept values, or values
 // recomputed from the row.  A replayed chunk is one whose running sum crosses
 // a binade (often several, early in the row), so the 32 adds are done
-// serially -- redundantly in every lane -- rather than by the warp-parallel
-// chain, whose steps end at every crossing.
+// serially -- redundantly in every lane, on values gathered into registers
+// first -- rather than by the warp-parallel chain, whose steps end at every
+// crossing.  Padding lanes add +0, which leaves s >= 0 unchanged.
 __device__ float replay_chunk(StreamSmem& sm, const Ctx& c, int t, uint32_t side_plus1, float s) {
     const int lane = threadIdx.x & 31;
     const int base = t * kSC;
     const int cnt = min(kSC, c.V - base);
-    if (side_plus1) {
-        const float* vals = sm.side[side_plus1 - 1];
-#pragma unroll 8
-        for (int i = 0; i < cnt; ++i) s = __fadd_rn(s, vals[i]);
-        return s;
-    }
-    const float e = (lane < cnt) ? exact_e(c, sm, __ldg(c.src + base + lane)) : 0.0f;
-    for (int i = 0; i < cnt; ++i) s = __fadd_rn(s, __shfl_sync(kFullMask, e, i));
+    float e = 0.0f;
+    if (lane < cnt) e = side_plus1 ? sm.side[side_plus1 - 1][lane] : exact_e(c, sm, __ldg(c.src + base + lane));
+    float v[kSC];
+#pragma unroll
+    for (int i = 0; i < kSC; ++i) v[i] = __shfl_sync(kFullMask, e, i);
+#pragma unroll
+    for (int i = 0; i < kSC; ++i) s = __fadd_rn(s, v[i]);
     return s;
 }
 
-// Exact serial softmax denominator from the chunk tables (warp 0).
-__device__ float resolve_S(StreamSmem& sm, const Ctx& c) {
-    const int lane = threadIdx.x & 31;
-    float s = 0.0f;
-    const int nseg = (c.nch + 31) / 32;
-    for (int seg = 0; seg < nseg; ++seg) {
-        const float4 wf = sm.wfn[seg];
-        const uint32_t wz = __float_as_uint(wf.z);
-        if (wz & kFClean) {
+// Exact serial walk over the chunks of segment seg from s (warp 0, every
+// lane the same values): a run chunk applies its whole run at once, other
+// chunks their own or their alternative-binade function; a chunk whose
+// function does not hold for s (its running sum leaves the binade, or the
+// binade guess was wrong) is replayed.
+__device__ float walk_segment(StreamSmem& sm, const Ctx& c, int seg, float s) {
+    const int cnt = min(32, c.nch - seg * 32);
+    int cpos = 0;
+    while (cpos < cnt) {
+        const int t = seg * 32 + cpos;
+        const float4 ent = sm.fn[t];
+        const uint32_t ez = __float_as_uint(ent.z);
+        if (ez & kFClean) {
             float s2 = s;
-            if (xm::chain_apply(s2, __float_as_uint(wf.w), xm::ChainFn{wf.x, wf.y, wz & 3u})) {
+            if (xm::chain_apply(s2, __float_as_uint(ent.w), xm::ChainFn{ent.x, ent.y, ez & 3u})) {
                 s = s2;
+                cpos = (ez & kFRun) ? (int)((ez >> 24) & 31u) + 1 : cpos + 1;
                 continue;
             }
         }
-        // chunk-level walk, picking per chunk the function of the current binade
-        const int cnt = min(32, c.nch - seg * 32);
-        const float4 ent = (lane < cnt) ? sm.fn[seg * 32 + lane] : make_float4(0, 0, 0, 0);
-        const uint32_t ez = __float_as_uint(ent.z);
-        float4 aent = make_float4(0, 0, 0, 0);
-        if (lane < cnt && (ez & kFAlt)) aent = sm.alt[(ez >> 8) & 0xFFu];
-        const uint32_t az = __float_as_uint(aent.z);
-        int cpos = 0;
-        while (cpos < cnt) {
-            if (regular_sum(s)) {
-                const uint32_t eb = xm::binade_of(s);
-                const bool use_p = (ez & kFClean) && __float_as_uint(ent.w) == eb;
-                const bool use_a = !use_p && (ez & kFAlt) && (az & kFClean) && __float_as_uint(aent.w) == eb;
-                const bool has = (lane >= cpos) && (lane < cnt) && (use_p || use_a);
-                xm::ChainFn f = xm::chain_identity();
-                if (has) f = use_p ? xm::ChainFn{ent.x, ent.y, ez & 3u} : xm::ChainFn{aent.x, aent.y, az & 3u};
-                const unsigned hm = __ballot_sync(kFullMask, has || lane < cpos);
-                const int fi = (~hm) ? (__ffs(~hm) - 1) : 32;
-                f = warp_incl_compose(f);
-                const float hi = __uint_as_float((eb + 1u) << 23);
-                const float L = (__float_as_uint(s) & 1u) ? f.L1 : f.L0;
-                const bool inb = (lane < cpos) || ((lane < fi) && (L <= __fsub_rn(hi, s)));
-                const unsigned inm = __ballot_sync(kFullMask, inb);
-                const int m = (~inm) ? (__ffs(~inm) - 1) : 32;  // chunks [cpos, m) resolve exactly
-                if (m > cpos) {
-                    s = __shfl_sync(kFullMask, __fadd_rn(s, L), m - 1);
-                    cpos = m;
-                }
-                if (cpos < cnt) {
-                    const uint32_t sp = __shfl_sync(kFullMask, ez >> 16, cpos);
-                    s = replay_chunk(sm, c, seg * 32 + cpos, sp, s);
-                    ++cpos;
-                }
-            } else {
-                const uint32_t sp = __shfl_sync(kFullMask, ez >> 16, cpos);
-                s = replay_chunk(sm, c, seg * 32 + cpos, sp, s);
+        if (ez & kFAlt) {
+            const float4 a = sm.alt[(ez >> 8) & 0xFFu];
+            float s2 = s;
+            if (xm::chain_apply(s2, __float_as_uint(a.w), xm::ChainFn{a.x, a.y, __float_as_uint(a.z) & 3u})) {
+                s = s2;
                 ++cpos;
+                continue;
             }
         }
+        s = replay_chunk(sm, c, t, (ez >> 16) & 0xFFu, s);
+        ++cpos;
+    }
+    return s;
+}
+
+// Exact serial softmax denominator from the chunk tables (warp 0).  Lane k
+// holds segment k's function (clean when its 32 chunks are one run); runs of
+// clean segments of one binade are composed (segmented suffix scan), so the
+// walk jumps over each run of segments at once and walks chunk by chunk only
+// where a binade boundary lies.
+__device__ float resolve_S(StreamSmem& sm, const Ctx& c) {
+    const int lane = threadIdx.x & 31;
+    const int nseg = (c.nch + 31) / 32;
+    const float4 wf = (lane < nseg) ? sm.wfn[lane] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const uint32_t wz = __float_as_uint(wf.z), web = __float_as_uint(wf.w);
+    const bool su = (lane < nseg) && (wz & kFClean);
+    const xm::ChainFn own = su ? xm::ChainFn{wf.x, wf.y, wz & 3u} : xm::chain_identity();
+    const bool su_n = __shfl_down_sync(kFullMask, (int)su, 1) != 0;
+    const uint32_t web_n = __shfl_down_sync(kFullMask, web, 1);
+    int run_end = lane;
+    const xm::ChainFn run = warp_run_suffix(own, su && lane < 31 && su_n && web_n == web, run_end);
+    float s = 0.0f;
+    int seg = 0;
+    while (seg < nseg) {
+        if (__shfl_sync(kFullMask, (int)su, seg)) {
+            const uint32_t eb = __shfl_sync(kFullMask, web, seg);
+            float s2 = s;
+            const xm::ChainFn R{__shfl_sync(kFullMask, run.L0, seg), __shfl_sync(kFullMask, run.L1, seg),
+                                __shfl_sync(kFullMask, run.pbits, seg)};
+            if (xm::chain_apply(s2, eb, R)) {
+                s = s2;
+                seg = __shfl_sync(kFullMask, run_end, seg) + 1;
+                continue;
+            }
+            s2 = s;
+            const xm::ChainFn O{__shfl_sync(kFullMask, own.L0, seg), __shfl_sync(kFullMask, own.L1, seg),
+                                __shfl_sync(kFullMask, own.pbits, seg)};
+            if (xm::chain_apply(s2, eb, O)) {
+                s = s2;
+                ++seg;
+                continue;
+            }
+        }
+        s = walk_segment(sm, c, seg, s);
+        ++seg;
     }
     return s;
 }
@@ -637,16 +689,27 @@ __device__ void sort_bins(StreamSmem& sm, unsigned long long* kb, int D, int K, 
     }
 }
 
-// The next row of this CTA.  With a counter, rows past the first gridDim.x
-// are handed out in order of demand: rows differ in cost (nucleus size, the
-// serial sums' binade crossings), and a fixed stride leaves the CTAs that drew
-// heavy rows finishing last.  Without one, the fixed stride.
-__device__ __forceinline__ int next_row(const RowLaunch& p, StreamSmem& sm, int row) {
-    if (!p.row_counter) return row + gridDim.x;
-    __syncthreads();  // every thread has read sm.next_row of the previous row
-    if (threadIdx.x == 0) sm.next_row = (int)gridDim.x + atomicAdd(p.row_counter, 1);
-    __syncthreads();
-    return sm.next_row;
+// Rows past the first gridDim.x are handed out in order of demand when a
+// counter is given: rows differ in cost (nucleus size, the serial sums'
+// binade crossings), and a fixed stride leaves the CTAs that drew heavy rows
+// finishing last.  A CTA claims its next row one row ahead (claim_next_row at
+// the start of iteration `it`, into slot (it + 1) & 1) so that the row's
+// logits can be prefetched into L2 while the current row is finished; the
+// slot written during an iteration is never the one read at its start.
+__device__ __forceinline__ void claim_next_row(const RowLaunch& p, StreamSmem& sm, int row, int it) {
+    if (threadIdx.x == 0)
+        sm.next_row[(it + 1) & 1] = p.row_counter ? (int)gridDim.x + atomicAdd(p.row_counter, 1) : row + gridDim.x;
+}
+__device__ __forceinline__ int next_row(StreamSmem& sm, int& it) {
+    __syncthreads();  // slot (it + 1) & 1 written
+    ++it;
+    return sm.next_row[it & 1];
+}
+
+// Bulk prefetch of a row's logits into L2 (one instruction; 16-byte aligned
+// address, a multiple of 16 bytes).
+__device__ __forceinline__ void prefetch_row_l2(const float* src, int V) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"((unsigned)V * 4u) : "memory");
 }
 
 __device__ void defer_row_s(const RowLaunch& p, int row) {
@@ -656,10 +719,43 @@ __device__ void defer_row_s(const RowLaunch& p, int row) {
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
-// Loads chunk t (32 floats) with eight independent 16-byte loads.
+// Eight consecutive floats.  A thread reads its own 128-byte chunk, so a
+// warp's load touches 32 lines; as one 32-byte vector (a whole sector) per
+// lane the sector is requested once, where two 16-byte loads of the same
+// sector issued apart each fetch it from L2 when L1 (small beside four CTAs'
+// shared memory) has dropped it in between.
+struct F8 {
+    float v[8];
+};
+__device__ __forceinline__ F8 ldg8(const float* p, bool v32) {
+    F8 r;
+    if (v32) {  // 32-byte aligned
+        asm("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+            : "=f"(r.v[0]), "=f"(r.v[1]), "=f"(r.v[2]), "=f"(r.v[3]), "=f"(r.v[4]), "=f"(r.v[5]), "=f"(r.v[6]),
+              "=f"(r.v[7])
+            : "l"(p));
+    } else {
+        const float4 a = ldg4(p), b = ldg4(p + 4);
+        r.v[0] = a.x, r.v[1] = a.y, r.v[2] = a.z, r.v[3] = a.w;
+        r.v[4] = b.x, r.v[5] = b.y, r.v[6] = b.z, r.v[7] = b.w;
+    }
+    return r;
+}
+
+// Loads chunk t (32 floats): four 32-byte loads in flight (eight 16-byte
+// ones when the rows are only 16-byte aligned or the chunk is partial).
 __device__ __forceinline__ void load_chunk(const Ctx& c, int t, float (&a)[kSC]) {
     const int base = t * kSC;
     const int cnt = min(kSC, c.V - base);  // multiple of 4 when > 0
+    if (c.v32 && cnt == kSC) {
+#pragma unroll
+        for (int g = 0; g < kSC / 8; ++g) {
+            const F8 x = ldg8(c.src + base + 8 * g, true);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[8 * g + i] = x.v[i];
+        }
+        return;
+    }
 #pragma unroll
     for (int g = 0; g < kSC / 4; ++g) {
         float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -684,10 +780,41 @@ __device__ __forceinline__ float div_lean(float l, const Ctx& c) {
 // divergence than the exp it saves), the chain sums in the primary (v0, v1)
 // and alternative (w0, w1) binade, candidate counts in the histogram, and the
 // values of kept chunks.  kGeneral: a partial chunk, or a row whose d range
-// reaches below the fast exp range.
-template <bool kGeneral>
+// reaches below the fast exp range.  kAlt: some chunk of the warp has an
+// alternative binade (else w0, w1 are left as they are).
+template <bool kGeneral, bool kAlt>
 __device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx& c, StreamSmem& sm, float e_min,
                                             float* keep, float& v0, float& v1, float& w0, float& w1) {
+    if (!kGeneral) {
+        // whole chunk: 8-float granules, two in flight ahead
+        F8 xa = ldg8(cp, c.v32), xb = ldg8(cp + 8, c.v32);
+#pragma unroll 1
+        for (int g = 0; g < kSC / 8; ++g) {
+            F8 xn;
+            if (g + 2 < kSC / 8) xn = ldg8(cp + 8 * (g + 2), c.v32);
+            F8 a = xa;
+            xa = xb;
+            xb = xn;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                const float d = __fsub_rn(div_lean(a.v[w], c), c.max_x);
+                const float e = xm::exp_normal_range(d, sm.exptab);
+                if (e >= e_min) atomicAdd(&sm.hist[bin_of(e)], 1);
+                a.v[w] = e;
+                v0 = __fadd_rn(v0, e);
+                v1 = __fadd_rn(v1, e);
+                if (kAlt) {
+                    w0 = __fadd_rn(w0, e);
+                    w1 = __fadd_rn(w1, e);
+                }
+            }
+            if (keep) {
+                reinterpret_cast<float4*>(keep)[2 * g] = make_float4(a.v[0], a.v[1], a.v[2], a.v[3]);
+                reinterpret_cast<float4*>(keep)[2 * g + 1] = make_float4(a.v[4], a.v[5], a.v[6], a.v[7]);
+            }
+        }
+        return;
+    }
     // three granules in flight: rotate qa <- qb <- qc <- load(g + 3)
     float4 qa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), qb = qa, qc = qa;
     if (!kGeneral || 0 < cnt) qa = ldg4(cp);
@@ -709,8 +836,10 @@ __device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx&
             a[w] = e;
             v0 = __fadd_rn(v0, e);
             v1 = __fadd_rn(v1, e);
-            w0 = __fadd_rn(w0, e);
-            w1 = __fadd_rn(w1, e);
+            if (kAlt) {
+                w0 = __fadd_rn(w0, e);
+                w1 = __fadd_rn(w1, e);
+            }
         }
         if (keep) reinterpret_cast<float4*>(keep)[g] = make_float4(a[0], a[1], a[2], a[3]);
         qa = qb;
@@ -730,9 +859,12 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
     // per-CTA L2-resident scratch for nuclei above the on-chip capacity
     unsigned long long* super = p.workspace + (long long)blockIdx.x * p.ws_stride;
 
-    for (int row = blockIdx.x; row < p.batch; row = next_row(p, sm, row)) {
+    int it = 0;
+    for (int row = blockIdx.x; row < p.batch; row = next_row(sm, it)) {
+        claim_next_row(p, sm, row, it);
         Ctx c;
         c.src = p.logits + (long long)row * p.ld;
+        c.v32 = p.vec32 != 0;
         c.V = V;
         c.nch = nch;
         c.T = p.temperature_rows ? p.temperature_rows[row] : p.temperature;
@@ -953,6 +1085,11 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
         // rows skip pass 2 (whose fast exp does not carry NaN through)
         const bool nan_row = isnan(s_approx);
         bool nan_any = false;
+        // guaranteed nucleus mass the selected candidates must carry: topp plus
+        // the fp32 drift bound, against S_approx scaled up by the 2^-7 margin
+        // that bounds its distance to the exact serial S
+        const float target = (topp + 4096.0f * 0x1p-24f + 1e-5f) * s_approx * 1.0078125f;
+
 #pragma unroll 1
         for (int sidx = 0; sidx < (nan_row ? 0 : kStrips); ++sidx) {
             const int t = sidx * kST + tid;
@@ -973,10 +1110,15 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
             const float alo = __uint_as_float(alt << 23), alo1 = __uint_as_float((alt << 23) | 1u);
             float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
             const float* cp = c.src + t * kSC;
-            if (cnt == kSC && !wide)
-                pass2_chunk<false>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
-            else if (valid)
-                pass2_chunk<true>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
+            const bool warp_alt = __any_sync(kFullMask, alt != 0u);
+            if (cnt == kSC && !wide) {
+                if (warp_alt)
+                    pass2_chunk<false, true>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
+                else
+                    pass2_chunk<false, false>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
+            } else if (valid) {
+                pass2_chunk<true, true>(cp, cnt, c, sm, e_min, keep, v0, v1, w0, w1);
+            }
             nan_any |= isnan(v0);
             // chunk functions (primary and alternative binade)
             const bool clean = valid && eb != 0u && (__float_as_uint(v0) >> 23) == eb && (__float_as_uint(v1) >> 23) == eb;
@@ -995,13 +1137,21 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 }
             }
             if (keep_idx >= 0) z |= (uint32_t)(keep_idx + 1) << 16;
-            if (valid) sm.fn[t] = make_float4(f.L0, f.L1, __uint_as_float(z), __uint_as_float(eb));
-            // segment (= warp within the strip) function when all chunks are
-            // clean in one binade
+            // run chunks take the composition to the end of their run; the
+            // segment (= warp within the strip) function is lane 0's when all
+            // 32 chunks form one run
+            const bool runc = valid && clean && !(z & kFAlt);
+            const bool runc_n = __shfl_down_sync(kFullMask, (int)runc, 1) != 0;
+            const uint32_t eb_n = __shfl_down_sync(kFullMask, eb, 1);
+            int run_end = lane;
+            const xm::ChainFn F = warp_run_suffix(runc ? f : xm::chain_identity(),
+                                                  runc && lane < 31 && runc_n && eb_n == eb, run_end);
+            if (runc) z = (z & ~3u) | F.pbits | kFRun | ((uint32_t)run_end << 24);
+            if (valid)
+                sm.fn[t] = make_float4(runc ? F.L0 : f.L0, runc ? F.L1 : f.L1, __uint_as_float(z), __uint_as_float(eb));
             const uint32_t eb0 = __shfl_sync(kFullMask, eb, 0);
-            const bool uni = __all_sync(kFullMask, !valid || (clean && eb == eb0 && !(z & kFAlt)));
-            const xm::ChainFn F = warp_incl_compose((valid && clean) ? f : xm::chain_identity());
-            if (lane == 31)
+            const bool uni = __all_sync(kFullMask, !valid || (runc && eb == eb0));
+            if (lane == 0)
                 sm.wfn[sidx * kSW + warp] =
                     make_float4(F.L0, F.L1, __uint_as_float(F.pbits | (uni ? kFClean : 0u)), __uint_as_float(eb0));
         }
@@ -1042,10 +1192,13 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
             if (p.probs_out) defer = true;  // the general kernel writes the NaN probabilities
             flags = kFlagNan | kFlagNoCand;
         } else {
+            int K = 0, D = kBins - 1;
+            bool all_cand = false, fits = true;
+            unsigned long long* kb = sm.kbuf;
+            {
             // ---- nucleus bins from the histogram: guaranteed mass of bins 0..D
-            // against topp plus the fp32 drift bound, with the approximate S
-            // scaled up by the 2^-7 margin that bounds its distance to the
-            // exact serial S (checked after the walk: a miss defers the row)
+            // against the target mass (checked after the walk: a miss defers
+            // the row)
             int h[kBinsPerThread];
             int hc = 0;
             float hm = 0.0f;
@@ -1059,7 +1212,6 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
             const ScanF ms = block_scan_f(hm, sm);
             int ctot;
             const int cex = block_scan_i(hc, sm, ctot) - hc;
-            const float target = (topp + 4096.0f * 0x1p-24f + 1e-5f) * s_approx * 1.0078125f;
             if (ms.incl >= target && ms.excl < target) {
                 float m = ms.excl;
                 int cc = cex, d = tid * kBinsPerThread + kBinsPerThread - 1;
@@ -1076,16 +1228,17 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 sm.ksel = cc;
             }
             __syncthreads();
-            int D = sm.dbin, K = sm.ksel;
-            const bool all_cand = D < 0;
+            D = sm.dbin;
+            K = sm.ksel;
+            all_cand = D < 0;
             if (all_cand) {
                 D = kBins - 1;
                 K = ctot;
             }
             // the nucleus lives on chip, or in the CTA's L2 scratch
-            unsigned long long* kb = (K <= kKCap) ? sm.kbuf : super;
+            kb = (K <= kKCap) ? sm.kbuf : super;
             // the L2 scratch holds any nucleus (ws_stride >= V + 4096 keys)
-            const bool fits = K <= p.ws_stride;
+            fits = K <= p.ws_stride;
             if (fits) {
                 // bin offsets (hist becomes the scatter cursor)
                 int run = cex;
@@ -1179,6 +1332,13 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 sort_bins(sm, kb, D, K, V);
             }
             __syncthreads();
+            }
+            // this row is no longer re-read: bring the next one into L2 for
+            // its first pass (streamed rows: V % 4 == 0, 16-byte aligned)
+            if (tid == 0) {
+                const int nr = sm.next_row[(it + 1) & 1];
+                if (nr < p.batch) prefetch_row_l2(p.logits + (long long)nr * p.ld, V);
+            }
             const float S = sm.fval;
             if (p.probs_out && !(!fits || sm.flag)) {
                 // the softmax sample() leaves in the buffer: p = fl(e/S) for
@@ -1267,19 +1427,20 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                     __syncthreads();
                 }
                 const int n0 = sm.n0;
+                const bool all_c = all_cand;
                 const bool big = n0 > kWalkDirect;
                 if (big) build_walk_fns(sm, kb, n0);  // all threads
                 if (warp == 0) {
                     int res = -1;
                     if (n0 == 0) {
-                        res = all_cand ? -2 : -1;
+                        res = all_c ? -2 : -1;
                     } else {
                         auto get = [&](int i) { return key_prob(kb[i]); };
                         float cum = 0.0f;
                         // llama2.c:1036-1043
                         int last = big ? walk_chunks(sm, kb, n0, topp, cum, sm.ck_s)
                                        : warp_chain(get, n0, cum, topp, sm.ck_s, sm.ck_pos, &sm.n_ck);
-                        if (last >= n0) last = all_cand ? n0 - 1 : -1;  // llama2.c:1037
+                        if (last >= n0) last = all_c ? n0 - 1 : -1;  // llama2.c:1037
                         if (last >= 0) {
                             const float r = __fmul_rn(coin, cum);  // llama2.c:1046
                             // llama2.c:1047-1054 adds the same p's in the same

@@ -306,6 +306,7 @@ int dispatch(const SamplerBatchConfig* cfg, const float* logits, int batch, long
         B2S_CUDA(cudaMemsetAsync(defer_count, 0, 2 * sizeof(int), stream));  // count and row counter
         b2s::RowLaunch q = p;
         q.row_counter = defer_count + 1;
+        q.vec32 = (((uintptr_t)logits & 31u) == 0 && (ld % 8) == 0) ? 1 : 0;
         q.workspace = stream_ws;
         q.ws_stride = (long long)stream_stride(V);
         q.stats = stats;
@@ -523,14 +524,20 @@ int sampler_batched(const SamplerBatchConfig* cfg, const float* logits, int batc
                     row_flags, workspace, workspace_bytes, (cudaStream_t)stream, 0);
 }
 
-// Fused variant: classifier GEMM (tcgen05) with the statistics epilogue,
-// then the streaming sampler fed by those statistics.
-int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, const void* wcls, int batch, int dim,
-                            const float* temperature_rows, const float* topp_rows, const float* coins,
-                            unsigned long long* rng_state, int* out_ids, float* logits_out, int* row_flags,
-                            void* stream) {
+}  // extern "C"
+
+namespace {
+// The fused call: classifier GEMM (tcgen05) with the statistics epilogue,
+// then the streaming sampler fed by those statistics.  With x_f32 (one or two
+// rows), the final RMSNorm of x is folded into the classifier kernel and
+// `hidden` is not used.
+int fused_call(const SamplerBatchConfig* cfg, const void* hidden, const float* x_f32, const float* norm_w,
+               const void* wcls, int batch, int dim, const float* temperature_rows, const float* topp_rows,
+               const float* coins, unsigned long long* rng_state, int* out_ids, float* logits_out, int* row_flags,
+               void* stream) {
     g_last_launches = 0;
-    if (!cfg || !hidden || !wcls || !out_ids) return fail(SAMPLER_E_INVALID, "null config, hidden, wcls or out_ids");
+    if (!cfg || !(hidden || x_f32) || !wcls || !out_ids)
+        return fail(SAMPLER_E_INVALID, "null config, hidden, wcls or out_ids");
     const int V = cfg->vocab_size;
     if (batch < 0 || dim < 8 || (dim % 8) != 0 || V < 32 || (V % 32) != 0)
         return fail(SAMPLER_E_INVALID, "bad sizes: batch=%d dim=%d (multiple of 8) vocab=%d (multiple of 32)", batch,
@@ -541,6 +548,8 @@ int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, c
     if (((uintptr_t)hidden & 15u) || ((uintptr_t)wcls & 15u) || ((uintptr_t)logits_out & 15u))
         return fail(SAMPLER_E_INVALID, "hidden, wcls and logits_out must be 16-byte aligned");
     if (batch == 0) return SAMPLER_OK;
+    if (x_f32 && (!norm_w || !b2s::gemm_folds_rmsnorm(batch, dim)))
+        return fail(SAMPLER_E_INVALID, "the folded RMSNorm takes one or two rows of dim <= 16384");
     DeviceCtx* c = nullptr;
     int rc = get_ctx(&c);
     if (rc) return rc;
@@ -577,12 +586,26 @@ int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, c
     g.temperature = cfg->temperature;
     g.temperature_rows = temperature_rows;
     g.error_word = c->error_word;
+    g.x_f32 = x_f32;
+    g.norm_w = norm_w;
     const int n = b2s::launch_classifier_gemm(g, c->num_sms, (cudaStream_t)stream);
     if (n < 0) return fail(SAMPLER_E_CUDA, "classifier GEMM launch: %s", cudaGetErrorString((cudaError_t)(-n)));
     rc = dispatch(cfg, logits, batch, V, temperature_rows, topp_rows, coins, rng_state, out_ids, nullptr, row_flags,
                   nullptr, 0, (cudaStream_t)stream, 0, stats, sld);
     g_last_launches += n;
     return rc;
+}
+}  // namespace
+
+extern "C" {
+
+int classifier_sample_fused(const SamplerBatchConfig* cfg, const void* hidden, const void* wcls, int batch, int dim,
+                            const float* temperature_rows, const float* topp_rows, const float* coins,
+                            unsigned long long* rng_state, int* out_ids, float* logits_out, int* row_flags,
+                            void* stream) {
+    if (!hidden) return fail(SAMPLER_E_INVALID, "null hidden");
+    return fused_call(cfg, hidden, nullptr, nullptr, wcls, batch, dim, temperature_rows, topp_rows, coins, rng_state,
+                      out_ids, logits_out, row_flags, stream);
 }
 
 // Final RMSNorm prologue alone: out_bf16[b, :] = bf16(weight * (x[b, :] / rms)).
@@ -607,6 +630,11 @@ int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* 
     if (!x || !norm_weight) return fail(SAMPLER_E_INVALID, "null x or norm_weight");
     if (batch < 0 || dim < 8 || (dim % 8) != 0) return fail(SAMPLER_E_INVALID, "bad sizes: batch=%d dim=%d", batch, dim);
     if (batch == 0) return SAMPLER_OK;
+    // one or two rows (decode): the classifier kernel forms the normalized
+    // operand itself -- one launch fewer, the same bits
+    if (b2s::gemm_folds_rmsnorm(batch, dim))
+        return fused_call(cfg, nullptr, x, norm_weight, wcls, batch, dim, temperature_rows, topp_rows, coins,
+                          rng_state, out_ids, logits_out, row_flags, stream);
     DeviceCtx* c = nullptr;
     int rc = get_ctx(&c);
     if (rc) return rc;

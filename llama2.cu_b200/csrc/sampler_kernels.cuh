@@ -38,6 +38,7 @@ struct RowLaunch {
     // streaming kernel: next row to take (rows handed out in order of demand
     // past the first gridDim.x); nullptr keeps the fixed stride
     int* row_counter;
+    int vec32;  // every row starts on a 32-byte boundary (32-byte chunk loads)
     // deferred rows: the streaming kernel appends rows it leaves to the
     // general kernel; the general kernel then walks row_list[0..*row_count)
     int* defer_count;
@@ -66,6 +67,12 @@ struct GemmLaunch {
     float temperature;
     const float* temperature_rows;
     int* error_word;
+    // Final RMSNorm folded into the one- or two-row classifier (GEMV): when
+    // x_f32 is set, h is ignored and each CTA forms the bf16 operand
+    // bf16(norm_w * (x / rms(x))) of the rows itself, bit-identical to
+    // launch_rmsnorm_bf16's output.
+    const float* x_f32;   // fp32 [batch, dim] or nullptr
+    const float* norm_w;  // fp32 [dim]
 };
 
 struct ArgmaxLaunch {
@@ -95,6 +102,9 @@ int launch_classifier_gemm(const GemmLaunch& p, int num_sms, cudaStream_t stream
 // The same GEMM by CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles).
 int launch_classifier_gemm_pair(const GemmLaunch& p, int num_sms, cudaStream_t stream);
 size_t gemm_smem_bytes();
+// Whether launch_classifier_gemm folds the final RMSNorm (x_f32 / norm_w) in:
+// the GEMV shapes (one or two rows) with dim up to 16384.
+bool gemm_folds_rmsnorm(int batch, int dim);
 // Final RMSNorm of `batch` fp32 rows into bf16 (the GEMM's A operand).
 int launch_rmsnorm_bf16(const float* x, const float* weight, int batch, int dim, void* out, cudaStream_t stream);
 // Embedding rows of the sampled ids (the next decode step's input).

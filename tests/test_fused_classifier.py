@@ -241,3 +241,38 @@ def test_device_logits_through_dump_files(pkg, orc, tmp_path):
     assert json.load(open(ip)) == ids.cpu().numpy().tolist()
     ref_ids, _, ref_p = orc.sample_batch(back, 0.8, 0.9, seeds, probs_out=True)
     check_e2e(orc, ids.cpu().numpy(), ref_ids, ref_p, seeds, np.full(B, 0.9))
+
+
+@pytest.mark.parametrize("B,D", [(1, 4096), (2, 4096), (1, 520), (2, 4104)])
+def test_rmsnorm_folded_into_decode_classifier(pkg, B, D):
+    """At decode batches (one or two rows) the final RMSNorm is folded into
+    the classifier kernel: the call launches one kernel fewer than
+    rmsnorm_bf16 followed by classifier_sample_fused, and gives the same
+    logits bit for bit (the fold repeats the norm kernel's arithmetic in its
+    order), hence the same ids and states."""
+    V = 32000
+    g = torch.Generator().manual_seed(61 + B + D)
+    x = (torch.randn(B, D, generator=g) * 3.0).to(DEV)
+    nw = (1.0 + 0.1 * torch.randn(D, generator=g)).to(DEV)
+    w = (torch.randn(V, D, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    seeds = pkg.workloads.row_seeds(B)
+    st1 = torch.from_numpy(seeds.view(np.int64).copy()).to(DEV)
+    st2 = st1.clone()
+    lg1 = torch.empty(B, V, device=DEV)
+    lg2 = torch.empty(B, V, device=DEV)
+    ids1 = pkg.classifier_rmsnorm_sample_fused(x, nw, w, 0.8, 0.9, st1, logits_out=lg1)
+    n_fold = pkg.last_launch_count()
+    h = pkg.rmsnorm_bf16(x, nw)
+    n_norm = pkg.last_launch_count()
+    ids2 = pkg.classifier_sample_fused(h, w, 0.8, 0.9, st2, logits_out=lg2)
+    n_fused = pkg.last_launch_count()
+    torch.cuda.synchronize()
+    assert n_fold == n_norm + n_fused - 1
+    assert torch.equal(lg1.view(torch.int32), lg2.view(torch.int32))
+    assert torch.equal(ids1, ids2) and torch.equal(st1, st2)
+    # the logits against an fp32 matmul of the fp32-normalized rows: within the
+    # bf16 rounding of the operand (2^-8 relative per product, summed)
+    ref_h = nw * (x * (1.0 / torch.sqrt((x * x).mean(dim=1, keepdim=True) + 1e-5)))
+    ref = ref_h @ w.float().t()
+    bound = ref_h.abs() @ w.float().abs().t()
+    assert bool(((lg1 - ref).abs() <= 2.0 ** -8 * bound + 1e-5).all())
