@@ -161,8 +161,9 @@ int sampler_batched(const SamplerBatchConfig* cfg, const float* logits, int batc
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Same as sampler_batched but every buffer is a HOST buffer; copies to and
- * from the device happen inside (pinned or pageable host memory).  Rows are
- * pipelined in chunks over two streams so copies overlap sampling.
+ * from the device happen inside (pinned or pageable host memory).  The rows
+ * are copied in up to 16 pieces back to back on one stream and sampled on
+ * another as each piece lands, so the copies overlap the sampling.
  * rng_state (host) is advanced in place. */
 int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int batch,
                          long long ld, const float* topp_rows, unsigned long long* rng_state,

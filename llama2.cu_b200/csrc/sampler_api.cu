@@ -72,7 +72,8 @@ struct DeviceCtx {
     int device = -1;
     int num_sms = 0;
     cudaStream_t stream = nullptr;   // used by the single-row llama2.c entry points
-    cudaStream_t streams[2] = {nullptr, nullptr};  // host-buffer pipeline
+    cudaStream_t streams[2] = {nullptr, nullptr};  // host-buffer pipeline: [0] copies in, [1] samples
+    cudaEvent_t piece_ready[16] = {};               // piece k of the pipeline is on the device
     int* error_word = nullptr;
     // single-row buffers (the llama2.c entry points, serialized by host_mu)
     unsigned long long* host_ws = nullptr;
@@ -112,6 +113,7 @@ int get_ctx(DeviceCtx** out) {
         B2S_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
         B2S_CUDA(cudaStreamCreateWithFlags(&c->streams[0], cudaStreamNonBlocking));
         B2S_CUDA(cudaStreamCreateWithFlags(&c->streams[1], cudaStreamNonBlocking));
+        for (cudaEvent_t& e : c->piece_ready) B2S_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         B2S_CUDA(cudaMalloc(&c->error_word, sizeof(int)));
         B2S_CUDA(cudaMemset(c->error_word, 0, sizeof(int)));
         B2S_CUDA(cudaMalloc(&c->d_coin, 4 * sizeof(float)));
@@ -716,14 +718,20 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
                             (cfg->temperature == 0.0f ||
                              ((cfg->flags & SAMPLER_FLAG_GREEDY_BELOW_1E6) && cfg->temperature < 1e-6f));
     if (!all_greedy && !rng_state) return fail(SAMPLER_E_INVALID, "rng_state is NULL");
-    // Each of the two pipeline streams gets its own half of the workspace so
-    // two chunks in flight never share slow-path scratch.
-    int chunk = (batch + 7) / 8;  // about eight chunks, each at least one CTA per SM
-    if (chunk < c->num_sms) chunk = batch < c->num_sms ? batch : c->num_sms;
-    const size_t ws_half = (workspace_for(c, V, chunk) + 255) & ~(size_t)255;
+    // Pipeline: one stream copies in -- the per-row inputs first, then the
+    // logits in up to 16 pieces back to back (pieces of tens of MB keep the
+    // host-to-device engine at its full rate, where one large copy runs
+    // slower and small copies or kernels between pieces leave it idle) -- and
+    // one stream samples each piece once it has landed and copies its ids and
+    // states back (the other direction's engine).  One stream samples, so one
+    // workspace serves every piece.
+    constexpr int kPieces = 16;
+    int piece = (batch + kPieces - 1) / kPieces;
+    if (piece < 1) piece = 1;
+    const size_t ws_bytes = (workspace_for(c, V, piece) + 255) & ~(size_t)255;
     {
         std::lock_guard<std::mutex> lk(g_mu);
-        rc = ensure_buf(&c->pipe_ws, &c->pipe_ws_bytes, 2 * ws_half);
+        rc = ensure_buf(&c->pipe_ws, &c->pipe_ws_bytes, ws_bytes);
         if (rc) return rc;
         const size_t need = (size_t)batch * (size_t)V;
         if (c->logits_cap < need) {
@@ -747,35 +755,41 @@ int sampler_batched_host(const SamplerBatchConfig* cfg, const float* logits, int
             c->rows_cap = batch;
         }
     }
-    // Chunks of rows alternate between two streams: the copy of chunk k+1
-    // overlaps the sampling of chunk k.
-    int launches = 0;
-    for (int r0 = 0, k = 0; r0 < batch; r0 += chunk, ++k) {
-        const int rows = (batch - r0) < chunk ? (batch - r0) : chunk;
-        cudaStream_t s = c->streams[k & 1];
+    cudaStream_t cs = c->streams[0], ks = c->streams[1];
+    if (topp_rows)
+        B2S_CUDA(cudaMemcpyAsync(c->d_topp, topp_rows, (size_t)batch * sizeof(float), cudaMemcpyHostToDevice, cs));
+    if (!all_greedy)
+        B2S_CUDA(cudaMemcpyAsync(c->d_state, rng_state, (size_t)batch * sizeof(unsigned long long),
+                                 cudaMemcpyHostToDevice, cs));
+    // every upload is queued before any copy back: a copy into pageable host
+    // memory returns only once done, and would hold back the next upload
+    for (int r0 = 0, k = 0; r0 < batch; r0 += piece, ++k) {
+        const int rows = (batch - r0) < piece ? (batch - r0) : piece;
         float* dl = c->d_logits + (size_t)r0 * V;
         if (ld == V) {
             B2S_CUDA(cudaMemcpyAsync(dl, logits + (size_t)r0 * V, (size_t)rows * V * sizeof(float),
-                                     cudaMemcpyHostToDevice, s));
+                                     cudaMemcpyHostToDevice, cs));
         } else {
             B2S_CUDA(cudaMemcpy2DAsync(dl, (size_t)V * sizeof(float), logits + (size_t)r0 * ld,
                                        (size_t)ld * sizeof(float), (size_t)V * sizeof(float), rows,
-                                       cudaMemcpyHostToDevice, s));
+                                       cudaMemcpyHostToDevice, cs));
         }
-        if (topp_rows)
-            B2S_CUDA(cudaMemcpyAsync(c->d_topp + r0, topp_rows + r0, rows * sizeof(float), cudaMemcpyHostToDevice, s));
-        if (!all_greedy)
-            B2S_CUDA(cudaMemcpyAsync(c->d_state + r0, rng_state + r0, rows * sizeof(unsigned long long),
-                                     cudaMemcpyHostToDevice, s));
-        void* ws = reinterpret_cast<char*>(c->pipe_ws) + (size_t)(k & 1) * ws_half;
+        B2S_CUDA(cudaEventRecord(c->piece_ready[k], cs));
+    }
+    int launches = 0;
+    for (int r0 = 0, k = 0; r0 < batch; r0 += piece, ++k) {
+        const int rows = (batch - r0) < piece ? (batch - r0) : piece;
+        float* dl = c->d_logits + (size_t)r0 * V;
+        B2S_CUDA(cudaStreamWaitEvent(ks, c->piece_ready[k], 0));
         rc = dispatch(cfg, dl, rows, V, nullptr, topp_rows ? c->d_topp + r0 : nullptr, nullptr,
-                      all_greedy ? nullptr : c->d_state + r0, c->d_ids + r0, nullptr, nullptr, ws, ws_half, s, 0);
+                      all_greedy ? nullptr : c->d_state + r0, c->d_ids + r0, nullptr, nullptr, c->pipe_ws, ws_bytes,
+                      ks, 0);
         if (rc) return rc;
         launches += g_last_launches;
-        B2S_CUDA(cudaMemcpyAsync(out_ids + r0, c->d_ids + r0, rows * sizeof(int), cudaMemcpyDeviceToHost, s));
+        B2S_CUDA(cudaMemcpyAsync(out_ids + r0, c->d_ids + r0, rows * sizeof(int), cudaMemcpyDeviceToHost, ks));
         if (!all_greedy)
             B2S_CUDA(cudaMemcpyAsync(rng_state + r0, c->d_state + r0, rows * sizeof(unsigned long long),
-                                     cudaMemcpyDeviceToHost, s));
+                                     cudaMemcpyDeviceToHost, ks));
     }
     B2S_CUDA(cudaStreamSynchronize(c->streams[0]));
     B2S_CUDA(cudaStreamSynchronize(c->streams[1]));
