@@ -220,7 +220,9 @@ int rmsnorm_bf16(const float* x, const float* norm_weight, int batch, int dim, v
 
 /* The whole decode step from the last layer's fp32 output: rmsnorm_bf16 into
  * a library-managed buffer, then classifier_sample_fused (same arguments and
- * results). */
+ * results).  For one or two rows with dim <= 16384 the normalization is done
+ * inside the classifier kernel instead (one launch, no intermediate buffer),
+ * with the same bits as the two-launch chain. */
 int classifier_rmsnorm_sample_fused(const SamplerBatchConfig* cfg, const float* x, const float* norm_weight,
                                     const void* wcls, int batch, int dim, const float* temperature_rows,
                                     const float* topp_rows, const float* coins, unsigned long long* rng_state,
