@@ -15,7 +15,7 @@ constexpr int kKCap = 2048;    // nucleus keys kept on chip (more spill to L2)
 constexpr int kSideCap = 48;   // chunks whose values are kept for replays
 constexpr int kAltCap = 96;    // chunks with an alternative-binade function
 constexpr int kBinsPerThread = kBins / kST;
-constexpr int kWalkDirect = 512;
+constexpr int kWalkDirect = 512;  // nuclei walked by the serial loop (their sums fit the chunk table)
 constexpr int kPairCap = 128;   // equal-p neighbour positions recorded for the tie fix  // nuclei walked element by element; larger ones by chunk functions
 
 // chunk entry: x=L0 y=L1 z=bits(pbits | flags | alt<<8 | side<<16 | run end<<24) w=bits(eb)
@@ -50,16 +50,15 @@ struct StreamSmem {
     int result;
     int n0;
     float fval;
-    // running sums of the first nucleus walk (cum > topp), where the second
-    // (r < cdf, the same serial sums) may resume: at segment starts (chunk
-    // walk) or at chain steps (ck_pos = element index)
+    // running sums of the first walk over a large nucleus (cum > topp) at
+    // segment starts, where the second (r < cdf, the same serial sums) may
+    // resume
     float ck_s[32];
-    int ck_pos[32];
-    int n_ck;
 };
 
 // RS_CTAS_PER_SM CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per CTA.
 static_assert(RS_CTAS_PER_SM * (sizeof(StreamSmem) + 1024) <= 228 * 1024, "StreamSmem too large");
+static_assert(kWalkDirect <= 4 * kChunks, "the serial walk records its sums in the chunk table");
 
 struct Ctx {
     const float* src;  // row
@@ -169,87 +168,6 @@ __device__ __forceinline__ xm::ChainFn warp_incl_compose(xm::ChainFn f) {
 __device__ __forceinline__ bool regular_sum(float s) {
     const uint32_t eb = xm::binade_of(s);
     return s > 0.0f && eb >= xm::kMinFastBinade && eb < 254u;
-}
-
-// ---------------------------------------------------------------------------
-// Warp-cooperative exact serial sum: s_i = fl(s_{i-1} + a_i) over i < n,
-// starting from the exact value s.  Returns the first i with s_i > theta
-// (s = s_i), or n (s = s_{n-1}).  With ck_s, the first 32 steps record
-// (element index, sum of the elements before it) in ck_pos / ck_s and their
-// count in *n_ck.  While s is a normal number well above
-// 2^-100, 32 addends are handled per step: each lane forms its addend's
-// chain function in the binade of s, an inclusive warp scan composes them,
-// and every lane whose running sum stays in that binade is exact; the addend
-// that leaves the binade is added for real.  Addends must be >= 0.
-// ---------------------------------------------------------------------------
-template <class Get>
-__device__ int warp_chain(const Get& get, int n, float& s, float theta, float* ck_s = nullptr,
-                          int* ck_pos = nullptr, int* n_ck = nullptr) {
-    const int lane = threadIdx.x & 31;
-    int pos = 0, nck = 0;
-    while (pos < n) {
-        if (ck_s && nck < 32) {  // checkpoint: s is the sum of elements [0, pos)
-            if (lane == 0) {
-                ck_s[nck] = s;
-                ck_pos[nck] = pos;
-                *n_ck = nck + 1;
-            }
-            ++nck;
-        }
-        const int i = pos + lane;
-        const float x = (i < n) ? get(i) : 0.0f;
-        if (regular_sum(s)) {
-            const uint32_t sb = __float_as_uint(s);
-            const uint32_t eb = (sb >> 23) & 0xFFu;
-            const float lo = __uint_as_float(eb << 23), lo1 = __uint_as_float((eb << 23) | 1u);
-            const float v0 = __fadd_rn(lo, x), v1 = __fadd_rn(lo1, x);
-            const bool ok = (i < n) && ((__float_as_uint(v0) >> 23) == eb) && ((__float_as_uint(v1) >> 23) == eb);
-            xm::ChainFn f = ok ? xm::ChainFn{__fsub_rn(v0, lo), __fsub_rn(v1, lo1),
-                                             (__float_as_uint(v0) & 1u) | ((__float_as_uint(v1) & 1u) << 1)}
-                               : xm::chain_identity();
-            const unsigned okm = __ballot_sync(kFullMask, ok);
-            const int fi = (~okm) ? (__ffs(~okm) - 1) : 32;
-            f = warp_incl_compose(f);
-            const float hi = __uint_as_float((eb + 1u) << 23);
-            const float L = (sb & 1u) ? f.L1 : f.L0;
-            const bool inb = (lane < fi) && (L <= __fsub_rn(hi, s));
-            const unsigned inm = __ballot_sync(kFullMask, inb);
-            const int m = (~inm) ? (__ffs(~inm) - 1) : 32;
-            const float sl = __fadd_rn(s, L);
-            const unsigned hit = __ballot_sync(kFullMask, (lane < m) && (sl > theta));
-            if (hit) {
-                const int h = __ffs(hit) - 1;
-                s = __shfl_sync(kFullMask, sl, h);
-                return pos + h;
-            }
-            if (m > 0) s = __shfl_sync(kFullMask, sl, m - 1);
-            const float a = __shfl_sync(kFullMask, x, m & 31);
-            pos += m;
-            if (m < 32 && pos < n) {
-                s = __fadd_rn(s, a);
-                if (s > theta) return pos;
-                pos += 1;
-            }
-        } else if (s == 0.0f) {
-            const unsigned nz = __ballot_sync(kFullMask, (i < n) && (x != 0.0f));
-            if (!nz) {
-                pos += 32;
-                continue;
-            }
-            const int z = __ffs(nz) - 1;
-            const float a = __shfl_sync(kFullMask, x, z);
-            pos += z;
-            s = __fadd_rn(s, a);
-            if (s > theta) return pos;
-            pos += 1;
-        } else {
-            const float a = __shfl_sync(kFullMask, x, 0);
-            s = __fadd_rn(s, a);
-            if (s > theta) return pos;
-            pos += 1;
-        }
-    }
-    return n;
 }
 
 // Exact e value of one logit.
@@ -768,6 +686,18 @@ __device__ __forceinline__ void load_chunk(const Ctx& c, int t, float (&a)[kSC])
 }
 
 
+// Counts e in its histogram bin (bin_of) when e >= e_min, without a branch:
+// one predicated shared-memory reduction.  A conditional atomicAdd splits the
+// unrolled element loop into one basic block per element, so the elements'
+// independent exp work cannot be interleaved.  e <= 1 here (d <= 0); NaN
+// fails the compare.
+__device__ __forceinline__ void hist_count(uint32_t hist_base, float e, float e_min) {
+    const uint32_t b = min((uint32_t)((int)kOneTop - (int)(__float_as_uint(e) >> kBinShift)), (uint32_t)(kBins - 1));
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ge.f32 p, %1, %2;\n\t@p red.shared.add.u32 [%0], 1;\n\t}" ::"r"(hist_base + (b << 2)),
+        "f"(e), "f"(e_min));
+}
+
 // x = l/T for the rows the kernel takes (see the lean-row rule in the kernel).
 __device__ __forceinline__ float div_lean(float l, const Ctx& c) {
     const float q = __fmul_rn(l, c.rT);
@@ -785,6 +715,7 @@ __device__ __forceinline__ float div_lean(float l, const Ctx& c) {
 template <bool kGeneral, bool kAlt>
 __device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx& c, StreamSmem& sm, float e_min,
                                             float* keep, float& v0, float& v1, float& w0, float& w1) {
+    const uint32_t hbase = smem_addr(sm.hist);
     if (!kGeneral) {
         // whole chunk: 8-float granules, two in flight ahead
         F8 xa = ldg8(cp, c.v32), xb = ldg8(cp + 8, c.v32);
@@ -799,7 +730,7 @@ __device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx&
             for (int w = 0; w < 8; ++w) {
                 const float d = __fsub_rn(div_lean(a.v[w], c), c.max_x);
                 const float e = xm::exp_normal_range(d, sm.exptab);
-                if (e >= e_min) atomicAdd(&sm.hist[bin_of(e)], 1);
+                hist_count(hbase, e, e_min);
                 a.v[w] = e;
                 v0 = __fadd_rn(v0, e);
                 v1 = __fadd_rn(v1, e);
@@ -831,7 +762,7 @@ __device__ __forceinline__ void pass2_chunk(const float* cp, int cnt, const Ctx&
             if (!kGeneral || 4 * g + w < cnt) {
                 const float d = __fsub_rn(div_lean(a[w], c), c.max_x);
                 e = kGeneral ? xm::exp_f32(d, sm.exptab) : xm::exp_normal_range(d, sm.exptab);
-                if (e >= e_min) atomicAdd(&sm.hist[bin_of(e)], 1);
+                hist_count(hbase, e, e_min);
             }
             a[w] = e;
             v0 = __fadd_rn(v0, e);
@@ -1434,35 +1365,81 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                     int res = -1;
                     if (n0 == 0) {
                         res = all_c ? -2 : -1;
+                    } else if (!big) {
+                        // llama2.c:1036-1043 as written: one serial fp32 sum,
+                        // run in every lane on broadcast reads (no shuffles);
+                        // lane 0 records each partial sum.  The chunk table is
+                        // free once S is resolved and holds up to 4 * kChunks
+                        // sums.
+                        // Groups of 8: the adds form one dependent chain (keys
+                        // past n0 add +0); the sums only grow, so a group holds
+                        // the crossing iff its last sum exceeds topp.
+                        float* cdf = reinterpret_cast<float*>(sm.fn);
+                        float cum = 0.0f;
+                        int last = n0;
+                        for (int i0 = 0; i0 < n0; i0 += 8) {
+                            float c8[8];
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) c8[u] = (i0 + u < n0) ? key_prob(kb[i0 + u]) : 0.0f;
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) {
+                                cum = __fadd_rn(cum, c8[u]);
+                                c8[u] = cum;
+                            }
+                            if (lane == 0) {
+                                float4* d4 = reinterpret_cast<float4*>(cdf + i0);  // i0 % 8 == 0
+                                d4[0] = make_float4(c8[0], c8[1], c8[2], c8[3]);
+                                d4[1] = make_float4(c8[4], c8[5], c8[6], c8[7]);
+                            }
+                            if (c8[7] > topp) {
+                                int u = 7;
+#pragma unroll
+                                for (int v = 6; v >= 0; --v)
+                                    if (c8[v] > topp) u = v;
+                                if (i0 + u < n0) {
+                                    last = i0 + u;
+                                    cum = c8[u];
+                                }
+                                break;
+                            }
+                        }
+                        if (last >= n0) last = all_c ? n0 - 1 : -1;  // llama2.c:1037
+                        if (last >= 0) {
+                            // llama2.c:1046-1055: the second loop adds the same
+                            // p's in the same order, so its cdf values are the
+                            // recorded sums; the answer is the first i <= last
+                            // with r < cdf[i], else last
+                            const float r = __fmul_rn(coin, cum);
+                            __syncwarp();
+                            int k = last;
+                            for (int b = 0; b <= last; b += 32) {
+                                const int i = b + lane;
+                                const unsigned m = __ballot_sync(kFullMask, i <= last && cdf[i] > r);
+                                if (m) {
+                                    k = b + __ffs(m) - 1;
+                                    break;
+                                }
+                            }
+                            res = key_index(kb[k]);
+                        }
                     } else {
-                        auto get = [&](int i) { return key_prob(kb[i]); };
+                        // large nuclei: the same two walks over chunk functions
                         float cum = 0.0f;
                         // llama2.c:1036-1043
-                        int last = big ? walk_chunks(sm, kb, n0, topp, cum, sm.ck_s)
-                                       : warp_chain(get, n0, cum, topp, sm.ck_s, sm.ck_pos, &sm.n_ck);
+                        int last = walk_chunks(sm, kb, n0, topp, cum, sm.ck_s);
                         if (last >= n0) last = all_c ? n0 - 1 : -1;  // llama2.c:1037
                         if (last >= 0) {
                             const float r = __fmul_rn(coin, cum);  // llama2.c:1046
                             // llama2.c:1047-1054 adds the same p's in the same
                             // order as the first walk, so it resumes at the
-                            // last checkpoint whose sum is <= r (no earlier
-                            // cdf can exceed r)
+                            // last segment checkpoint whose sum is <= r (no
+                            // earlier cdf can exceed r)
                             __syncwarp();
-                            int k;
-                            if (big) {
-                                const int seg_last = last / (32 * kSC);
-                                const unsigned okm = __ballot_sync(kFullMask, lane <= seg_last && !(sm.ck_s[lane] > r));
-                                const int seg0 = 31 - __clz(okm);  // segment 0 (sum 0) always qualifies
-                                float s3 = 0.0f;
-                                k = walk_chunks(sm, kb, last + 1, r, s3, nullptr, seg0, sm.ck_s[seg0]);
-                            } else {
-                                const unsigned okm = __ballot_sync(
-                                    kFullMask, lane < sm.n_ck && sm.ck_pos[lane] <= last && !(sm.ck_s[lane] > r));
-                                const int q = 31 - __clz(okm);  // checkpoint 0 (pos 0, sum 0) always qualifies
-                                const int p0 = sm.ck_pos[q];
-                                float s3 = sm.ck_s[q];
-                                k = p0 + warp_chain([&](int i) { return key_prob(kb[p0 + i]); }, last + 1 - p0, s3, r);
-                            }
+                            const int seg_last = last / (32 * kSC);
+                            const unsigned okm = __ballot_sync(kFullMask, lane <= seg_last && !(sm.ck_s[lane] > r));
+                            const int seg0 = 31 - __clz(okm);  // segment 0 (sum 0) always qualifies
+                            float s3 = 0.0f;
+                            int k = walk_chunks(sm, kb, last + 1, r, s3, nullptr, seg0, sm.ck_s[seg0]);
                             if (k > last) k = last;  // llama2.c:1055
                             res = key_index(kb[k]);
                         }
