@@ -15,8 +15,8 @@ constexpr int kKCap = 2048;    // nucleus keys kept on chip (more spill to L2)
 constexpr int kSideCap = 48;   // chunks whose values are kept for replays
 constexpr int kAltCap = 96;    // chunks with an alternative-binade function
 constexpr int kBinsPerThread = kBins / kST;
-constexpr int kWalkDirect = 512;  // nuclei walked by the serial loop (their sums fit the chunk table)
-constexpr int kPairCap = 128;   // equal-p neighbour positions recorded for the tie fix  // nuclei walked element by element; larger ones by chunk functions
+constexpr int kWalkDirect = 1024;  // nuclei walked by the serial loop (their sums fit the chunk table)
+constexpr int kPairCap = 128;   // equal-p neighbour positions recorded for the tie fix
 
 // chunk entry: x=L0 y=L1 z=bits(pbits | flags | alt<<8 | side<<16 | run end<<24) w=bits(eb)
 // A run chunk (kFRun) is clean in its guessed binade with no alternative; its
@@ -186,8 +186,21 @@ __device__ float replay_chunk(StreamSmem& sm, const Ctx& c, int t, uint32_t side
     const int lane = threadIdx.x & 31;
     const int base = t * kSC;
     const int cnt = min(kSC, c.V - base);
+    if (side_plus1) {
+        // kept values (zero past cnt): every lane reads the same 16 bytes
+        const float4* kv = reinterpret_cast<const float4*>(sm.side[side_plus1 - 1]);
+#pragma unroll
+        for (int q = 0; q < kSC / 4; ++q) {
+            const float4 x = kv[q];
+            s = __fadd_rn(s, x.x);
+            s = __fadd_rn(s, x.y);
+            s = __fadd_rn(s, x.z);
+            s = __fadd_rn(s, x.w);
+        }
+        return s;
+    }
     float e = 0.0f;
-    if (lane < cnt) e = side_plus1 ? sm.side[side_plus1 - 1][lane] : exact_e(c, sm, __ldg(c.src + base + lane));
+    if (lane < cnt) e = exact_e(c, sm, __ldg(c.src + base + lane));
     float v[kSC];
 #pragma unroll
     for (int i = 0; i < kSC; ++i) v[i] = __shfl_sync(kFullMask, e, i);
@@ -1393,12 +1406,16 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                             }
                             if (c8[7] > topp) {
                                 int u = 7;
+                                float cu = c8[7];
 #pragma unroll
                                 for (int v = 6; v >= 0; --v)
-                                    if (c8[v] > topp) u = v;
+                                    if (c8[v] > topp) {
+                                        u = v;
+                                        cu = c8[v];
+                                    }
                                 if (i0 + u < n0) {
                                     last = i0 + u;
-                                    cum = c8[u];
+                                    cum = cu;
                                 }
                                 break;
                             }
