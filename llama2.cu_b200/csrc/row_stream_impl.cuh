@@ -1,6 +1,7 @@
 // row_stream_impl.cuh -- body of the streaming top-p kernel, included by
 // row_stream.cu once per CTA shape (RS_THREADS threads, RS_CTAS_PER_SM CTAs
-// per SM, RS_SORT_GROUP bins per sort group, in namespace b2s::RS_NS).  The
+// per SM, RS_SORT_GROUP bins per sort group, RS_KEY_CAP nucleus keys on chip,
+// in namespace b2s::RS_NS).  The
 // algorithm is described in row_stream.cu.
 namespace RS_NS {
 namespace {
@@ -11,7 +12,7 @@ constexpr int kSC = 32;        // elements per chunk
 constexpr int kChunks = 1024;  // chunks of 32 (V <= 32768)
 constexpr int kStrips = kChunks / kST;  // chunks per thread (strip s: chunk kST*s + t)
 constexpr int kSegs = kChunks / 32;         // 32 segments of 32 chunks
-constexpr int kKCap = 2048;    // nucleus keys kept on chip (more spill to L2)
+constexpr int kKCap = RS_KEY_CAP;  // nucleus keys kept on chip (more spill to L2)
 constexpr int kSideCap = 48;   // chunks whose values are kept for replays
 constexpr int kAltCap = 96;    // chunks with an alternative-binade function
 constexpr int kBinsPerThread = kBins / kST;
@@ -295,8 +296,9 @@ __device__ float resolve_S(StreamSmem& sm, const Ctx& c) {
 
 // All threads: chunk t = sorted keys [32t, 32t + 32) of the first n0; its
 // incoming cumulative sum is guessed from a block scan of approximate chunk
-// sums.  Fills fn / alt / wfn (free again once S is resolved).
-__device__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int n0) {
+// sums.  Fills fn / alt / wfn (free again once S is resolved).  Out of line:
+// inlined, it raised the kernel's register demand into spills.
+__device__ __noinline__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int n0) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nchk = (n0 + kSC - 1) / kSC;
     if (tid == 0) sm.n_alt = 0;
