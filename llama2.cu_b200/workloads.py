@@ -18,7 +18,7 @@ workloads).
                generator, SeedSequence(3, spawn_key=(r,)), so any range of
                global rows (a rank's shard of a multi-GPU batch) is drawn
                without drawing the rows before it.  Nucleus sizes of the first
-               4096 rows span 1 to about 2400 tokens (tests/golden/topp.json).
+               4096 rows span 1 to 2683 tokens, mean 156 (tests/golden/topp.json).
   fused        hidden [8192, 4096] bf16 ~ N(0, 1), seed 4; wcls [32000, 4096]
                bf16 ~ N(0, 0.02^2); T=0.8, topp=0.9.
 """
