@@ -8,7 +8,7 @@
 // chunk 256s + t of strip s; nuclei of up to 2048 keys stay in shared
 // memory, larger ones go to the CTA's L2-resident scratch.  Batches up to
 // the SM count (decode): one 1024-thread CTA per SM, one chunk per thread,
-// so each row's parallel phases use a whole SM, and nuclei of up to 16384
+// so each row's parallel phases use a whole SM, and nuclei of up to 14336
 // keys stay in its shared memory.  Rows past the first wave are handed out
 // by a device counter.  A thread's 128-byte chunk is read as 32-byte
 // vectors.
@@ -69,7 +69,7 @@ namespace b2s {
 #define RS_THREADS 1024
 #define RS_CTAS_PER_SM 1
 #define RS_SORT_GROUP 8
-#define RS_KEY_CAP 16384
+#define RS_KEY_CAP 14336
 #define RS_NS rs1024
 #include "row_stream_impl.cuh"
 #undef RS_NS

@@ -13,6 +13,12 @@ constexpr int kChunks = 1024;  // chunks of 32 (V <= 32768)
 constexpr int kStrips = kChunks / kST;  // chunks per thread (strip s: chunk kST*s + t)
 constexpr int kSegs = kChunks / 32;         // 32 segments of 32 chunks
 constexpr int kKCap = RS_KEY_CAP;  // nucleus keys kept on chip (more spill to L2)
+// Shapes with a large on-chip nucleus also keep its p values with each chunk
+// of 32 padded to 33 floats, so that thread t reading value j of chunk t hits
+// bank (t + j) mod 32 (the keys themselves, 256 bytes per chunk, put every
+// thread of a warp on one bank).
+constexpr bool kPadP = kKCap > 4096;
+constexpr int kPadPLen = kPadP ? ((kKCap / kSC) * (kSC + 1) + 3) / 4 * 4 : 4;  // whole 16-byte units
 constexpr int kSideCap = 48;   // chunks whose values are kept for replays
 constexpr int kAltCap = 96;    // chunks with an alternative-binade function
 constexpr int kBinsPerThread = kBins / kST;
@@ -28,9 +34,10 @@ constexpr uint32_t kFClean = 4u, kFValid = 8u, kFAlt = 16u, kFRun = 32u;
 
 struct StreamSmem {
     unsigned long long kbuf[kKCap];
+    float padp[kPadPLen];  // p of key i at (i / 32) * 33 + i % 32 (kPadP shapes)
     int hist[kBins];
     unsigned short bstart[kBins];  // bin offsets in the nucleus (< 2^16)
-    float side[kSideCap][kSC];
+    alignas(16) float side[kSideCap][kSC];  // read and written as float4
     float4 fn[kChunks];
     float4 alt[kAltCap];
     float4 wfn[kSegs];
@@ -60,6 +67,10 @@ struct StreamSmem {
 // RS_CTAS_PER_SM CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per CTA.
 static_assert(RS_CTAS_PER_SM * (sizeof(StreamSmem) + 1024) <= 228 * 1024, "StreamSmem too large");
 static_assert(kWalkDirect <= 4 * kChunks, "the serial walk records its sums in the chunk table");
+static_assert(offsetof(StreamSmem, side) % 16 == 0 && offsetof(StreamSmem, fn) % 16 == 0 &&
+                  offsetof(StreamSmem, alt) % 16 == 0 && offsetof(StreamSmem, wfn) % 16 == 0 &&
+                  offsetof(StreamSmem, kbuf) % 16 == 0,
+              "members accessed as float4 / 16-byte units must be 16-byte aligned");
 
 struct Ctx {
     const float* src;  // row
@@ -296,9 +307,10 @@ __device__ float resolve_S(StreamSmem& sm, const Ctx& c) {
 
 // All threads: chunk t = sorted keys [32t, 32t + 32) of the first n0; its
 // incoming cumulative sum is guessed from a block scan of approximate chunk
-// sums.  Fills fn / alt / wfn (free again once S is resolved).  Out of line:
-// inlined, it raised the kernel's register demand into spills.
-__device__ __noinline__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, int n0) {
+// sums.  Fills fn / alt / wfn (free again once S is resolved).  padp: the
+// nucleus's p values in the padded layout, or null (read the keys).  Out of
+// line: inlined, it raised the kernel's register demand into spills.
+__device__ __noinline__ void build_walk_fns(StreamSmem& sm, const unsigned long long* kb, const float* padp, int n0) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nchk = (n0 + kSC - 1) / kSC;
     if (tid == 0) sm.n_alt = 0;
@@ -310,7 +322,7 @@ __device__ __noinline__ void build_walk_fns(StreamSmem& sm, const unsigned long 
         if (t < nchk) {
             const int cnt = min(kSC, n0 - kSC * t);
 #pragma unroll 8  // loads in flight from the L2 scratch
-            for (int j = 0; j < cnt; ++j) a += key_prob(kb[kSC * t + j]);
+            for (int j = 0; j < cnt; ++j) a += padp ? padp[(kSC + 1) * t + j] : key_prob(kb[kSC * t + j]);
         }
         sig[sidx] = a;
     }
@@ -333,7 +345,7 @@ __device__ __noinline__ void build_walk_fns(StreamSmem& sm, const unsigned long 
         float v0 = lo, v1 = lo1, w0 = alo, w1 = alo1;
 #pragma unroll 8
         for (int j = 0; j < cnt; ++j) {
-            const float x = key_prob(kb[kSC * t + j]);
+            const float x = padp ? padp[(kSC + 1) * t + j] : key_prob(kb[kSC * t + j]);
             v0 = __fadd_rn(v0, x);
             v1 = __fadd_rn(v1, x);
             w0 = __fadd_rn(w0, x);
@@ -1342,8 +1354,13 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                     }
                     __syncthreads();  // every key of this round read before any is rewritten
 #pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        if (i0 + u * kST < K) kb[i0 + u * kST] = k[u];
+                    for (int u = 0; u < 4; ++u) {
+                        const int i = i0 + u * kST;
+                        if (i < K) {
+                            kb[i] = k[u];
+                            if (kPadP && kb == sm.kbuf) sm.padp[(i >> 5) * (kSC + 1) + (i & 31)] = key_prob(k[u]);
+                        }
+                    }
                 }
                 // equal-p runs (sorted by e, so contiguous) go to index order,
                 // glibc qsort's order for ties; runs are a few keys, found from
@@ -1375,7 +1392,7 @@ __global__ void __launch_bounds__(kST, RS_CTAS_PER_SM) row_stream_kernel(RowLaun
                 const int n0 = sm.n0;
                 const bool all_c = all_cand;
                 const bool big = n0 > kWalkDirect;
-                if (big) build_walk_fns(sm, kb, n0);  // all threads
+                if (big) build_walk_fns(sm, kb, (kPadP && kb == sm.kbuf) ? sm.padp : nullptr, n0);  // all threads
                 if (warp == 0) {
                     int res = -1;
                     if (n0 == 0) {
