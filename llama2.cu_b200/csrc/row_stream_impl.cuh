@@ -439,13 +439,33 @@ __device__ int walk_fns(const StreamSmem& sm, int n, float theta, float& cum, co
             if (cpos < cnt) {
                 const int base = (seg * 32 + cpos) * kSC;
                 const int ne = min(kSC, n - base);
-                // the crossing chunk: 32 serial adds (one coalesced load, shuffles)
+                // the crossing chunk: 32 serial adds (one coalesced load),
+                // 16 values gathered at a time and added as one dependent
+                // chain; the sums only grow, so a group holds the crossing
+                // of theta iff its last sum does (padding lanes add +0, so
+                // the first crossing is a real element)
                 const float x = (lane < ne) ? get(base + lane) : 0.0f;
-                for (int i = 0; i < ne; ++i) {
-                    s = __fadd_rn(s, __shfl_sync(kFullMask, x, i));
-                    if (s > theta) {
-                        cum = s;
-                        return base + i;
+#pragma unroll
+                for (int h = 0; h < kSC / 16; ++h) {
+                    float c16[16];
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) c16[q] = __shfl_sync(kFullMask, x, 16 * h + q);
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        s = __fadd_rn(s, c16[q]);
+                        c16[q] = s;
+                    }
+                    if (c16[15] > theta) {
+                        int u = 15;
+                        float cu = c16[15];
+#pragma unroll
+                        for (int v = 14; v >= 0; --v)
+                            if (c16[v] > theta) {
+                                u = v;
+                                cu = c16[v];
+                            }
+                        cum = cu;
+                        return base + 16 * h + u;
                     }
                 }
                 ++cpos;
