@@ -189,6 +189,20 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def host_cpu():
+    """The host's CPU model and logical CPU count (as nproc reports them)."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return dict(cpu_model=model, nproc=os.cpu_count())
+
+
 def cpu_baseline(x, topp_rows, rows, use_ref=True, min_seconds=10.0):
     """The reference's own sampler on all host threads: passes over the first
     `rows` rows of the workload, repeated until at least `min_seconds` of CPU
@@ -211,7 +225,7 @@ def cpu_baseline(x, topp_rows, rows, use_ref=True, min_seconds=10.0):
             break
     return dict(value=passes * rows / dt, unit="tokens/s", cores=threads, kind=kind,
                 sample=f"{passes} passes over {rows} rows of the top-p workload (llama2.c sample() per row, "
-                       f"OpenMP over rows), {dt:.1f} s")
+                       f"OpenMP over rows), {dt:.1f} s", **host_cpu())
 
 
 def run_reference(args):
@@ -241,7 +255,8 @@ def run_reference(args):
                 data="synthetic (seeded numpy PCG64)", impl="reference",
                 config=dict(workload=WORKLOAD, rows_per_step=rows, vocab=VOCAB, parallelism="host threads"),
                 cpu_baseline=dict(value=value, unit="tokens/s", cores=threads, kind=kind,
-                                  sample=f"{rows} rows per step, llama2.c sample() per row, OpenMP over rows"),
+                                  sample=f"{rows} rows per step, llama2.c sample() per row, OpenMP over rows",
+                                  **host_cpu()),
                 e2e=dict(value=value, unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
     return 0
