@@ -295,6 +295,12 @@ EDGE = [
     ("tiny_vocab", lambda r: np.random.default_rng(10).normal(0, 1, (r, 3)).astype(np.float32), 1.0, 0.5),
     ("max_vocab", lambda r: np.random.default_rng(13).normal(0, 2, (r, 32768)).astype(np.float32), 0.7, 0.95),
     ("negative_temperature", lambda r: np.random.default_rng(9).normal(0, 1, (r, 301)).astype(np.float32), -0.5, 0.9),
+    # full vocabulary: the streaming kernel's own path for T < 0 (the row's
+    # minimum plays the maximum's part once divided by T)
+    ("negative_temperature_wide", lambda r: np.random.default_rng(25).normal(0, 2, (r, 32000)).astype(np.float32),
+     -0.7, 0.9),
+    ("negative_temperature_mult", lambda r: np.random.default_rng(26).normal(0, 1.5, (r, 32000)).astype(np.float32),
+     -0.9, 1.0),
     ("huge_logits", lambda r: np.random.default_rng(14).normal(0, 60, (r, 4000)).astype(np.float32), 1.0, 0.9),
 ]
 
