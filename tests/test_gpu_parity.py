@@ -378,6 +378,24 @@ def test_unaligned_row_stride(pkg, orc):
     check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, np.full(20, 0.9))
 
 
+@pytest.mark.parametrize("want_probs", [False, True])
+def test_partial_last_chunk_and_16_byte_rows(pkg, orc, want_probs):
+    """The streaming kernel with V = 32004 (its last chunk of 32 holds 4
+    values) and a row stride of 32012 floats (rows 16- but not 32-byte
+    aligned, so chunks load as 16-byte vectors)."""
+    x = np.random.default_rng(27).normal(0, 2, (24, 32004)).astype(np.float32)
+    seeds = np.arange(24, dtype=np.uint64) * 3 + 1
+    topps = np.where(np.arange(24) % 3 == 0, 1.0, 0.9).astype(np.float32)
+    out = gpu_sample(pkg, x, 0.8, 0.9, seeds=seeds, topp_rows=topps, ld=32012, want_probs=want_probs)
+    ref_ids, ref_st, ref_p = orc.sample_batch(x, 0.8, 0.9, seeds, topp_rows=topps, probs_out=True)
+    assert np.array_equal(out["states"], ref_st)
+    assert not (out["flags"] & pkg.ROW_SLOW_PATH).any()
+    if want_probs:
+        rel, zero_ok = prob_rel_err(out["probs"], ref_p)
+        assert rel <= PROB_RTOL and zero_ok, rel
+    check_e2e(orc, out["ids"], ref_ids, ref_p, seeds, topps)
+
+
 def test_host_buffer_entry_point(pkg, orc):
     w = pkg.workloads.topp(rows=700)
     st = pkg.workloads.row_seeds(700)
